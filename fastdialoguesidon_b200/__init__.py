@@ -1,0 +1,32 @@
+"""fastdialoguesidon_b200: the FastDialogueSidon attention hot path on B200.
+
+Public API (mirrors the attention ops of ``fds_triton.kernels``):
+
+- :func:`flexrel_attention` / :func:`flexrel_attention_split` /
+  :func:`encoder_attention`: w2v-BERT relative_key self-attention;
+- :func:`rope_attention`: the DiT head's RoPE self-attention (replaces
+  ``rope_split`` + SDPA), and :func:`rope_split` itself;
+- :func:`check_status`: raise if a kernel reported a bounded-wait timeout.
+
+The same ops are registered as ``torch.ops.fds.flexrel_attention`` and
+``torch.ops.fds.rope_attention`` (see :mod:`.torch_ops`).
+"""
+
+from .kernels import (  # noqa: F401
+    LEFT,
+    NUM_POS,
+    NUM_POS_PAD,
+    RIGHT,
+    FdsError,
+    check_status,
+    cudnn_attention_available,
+    encoder_attention,
+    flexrel_attention,
+    flexrel_attention_split,
+    rope_attention,
+    rope_split,
+    rope_tables,
+)
+from . import torch_ops  # noqa: F401  (registers torch.ops.fds.*)
+
+__version__ = "0.1.0"

@@ -1,0 +1,533 @@
+// attn_kernel.cuh - sm_100a attention forward with an optional relative_key bias.
+//
+// One CTA owns 256 query rows of one (window, head): two 128-row query tiles
+// (Q0, Q1) that share every K/V tile. Warp roles (320 threads):
+//   warps 0-3  softmax for Q0 (thread = query row = TMEM lane)
+//   warps 4-7  softmax for Q1
+//   warp  8    MMA issuer (one thread) and TMEM owner
+//   warp  9    TMA producer (one thread)
+// TMEM (512 columns): S0 [0,128)  S1 [128,256)  O0 [256,320)  O1 [320,384).
+// P (the exponentiated scores, 16-bit) overwrites the first 64 columns of its
+// S tile and feeds the P.V product straight from TMEM.
+//
+// Relative bias (encoder): bias(i, j) = q_i . rel[clamp(j - i, -64, 8) + 64].
+// Per query tile the MMA computes QR = Q . rel^T (N = 80, rows 73..79 zero)
+// into the S columns once; the softmax threads copy their row of QR (scaled to
+// log2 units) into shared memory. A KV tile whose every (i, j) pair saturates
+// the clamp adds a per-row constant (QR[i,0] on the left, QR[i,72] on the
+// right), which folds into the exponent's FFMA offset at no per-score cost;
+// only the (at most three) near-diagonal tiles gather the bias per score.
+// This is the clamp-saturation property the reference exploits in
+// triton/src/fds_triton/kernels.py:364-398 (its _flexrel_kernel), realised
+// here as a per-tile offset instead of running-max shifts.
+//
+// Online softmax: log2 units, lazy rescaling (the running max used for the
+// exponent only moves when a tile's max exceeds it by more than 8, i.e. P is
+// bounded by 256), fp32 row sums, P rounded to the operand type.
+//
+// Every wait is bounded by a globaltimer deadline; an expired wait records a
+// status bit, raises a CTA-wide abort flag, and every role then drains its
+// in-flight copies / MMAs and exits so the context stays usable.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "fds_b200.h"
+#include "fds_ptx.cuh"
+
+namespace fds {
+
+constexpr int kBlockM = 128;       // query rows per tile (= TMEM lanes)
+constexpr int kQTiles = 2;         // query tiles per CTA
+constexpr int kRowsPerCta = kBlockM * kQTiles;
+constexpr int kBlockN = 128;       // keys per KV tile
+constexpr int kHeadDim = 64;
+constexpr int kStages = 3;         // K/V shared-memory ring depth
+constexpr int kTileBytes = kBlockM * kHeadDim * 2;
+constexpr int kNumPos = 73;        // relative-key table rows
+constexpr int kClampLeft = 64;
+constexpr int kClampRight = 8;
+constexpr int kRelRows = 80;       // table rows padded to a multiple of 16 (MMA N)
+constexpr int kQrStride = 74;      // floats per row of the shared QR copy (conflict-free gather)
+constexpr int kMmaWarp = 8;
+constexpr int kLoadWarp = 9;
+constexpr int kThreads = 320;
+constexpr int kTmemCols = 512;
+constexpr int kTmemO = 256;        // first O column
+constexpr float kRescaleThreshold = 8.0f;
+constexpr int64_t kDefaultTimeoutNs = 2000000000LL;
+
+struct Smem {
+    static constexpr int q0 = 0;
+    static constexpr int q1 = q0 + kTileBytes;
+    static constexpr int rel = q1 + kTileBytes;
+    static constexpr int k = rel + kRelRows * 128;            // 1024-aligned
+    static constexpr int v = k + kStages * kTileBytes;
+    static constexpr int qr = v + kStages * kTileBytes;
+    static constexpr int bars = qr + kRowsPerCta * kQrStride * 4;
+    // barrier indices
+    static constexpr int kQ = 0;
+    static constexpr int kKFull = 1;
+    static constexpr int kVFull = kKFull + kStages;
+    static constexpr int kKvEmpty = kVFull + kStages;
+    static constexpr int kSFull = kKvEmpty + kStages;
+    static constexpr int kPFull = kSFull + 2;
+    static constexpr int kODone = kPFull + 2;
+    static constexpr int kDrain = kODone + 2;
+    static constexpr int kNever = kDrain + 1;
+    static constexpr int kNumBars = kNever + 1;
+    static constexpr int misc = bars + kNumBars * 8;
+    static constexpr int total = misc + 16;
+    static constexpr int alloc = total + 1024;  // slack for 1024-byte alignment
+};
+static_assert(Smem::k % 1024 == 0 && Smem::v % 1024 == 0 && Smem::rel % 1024 == 0, "swizzle atoms");
+static_assert(Smem::alloc <= 232448, "shared memory budget");
+
+struct AttnParams {
+    void* out;
+    int64_t out_stride;       // elements
+    const int32_t* kv_len;    // [batch] or null
+    int32_t* status;          // or null
+    int64_t timeout_ns;
+    int32_t heads;
+    int32_t seq_len;
+    int32_t q_x0, k_x0, v_x0; // column (elements) of head 0's q / k / v in their maps
+    float scale_log2;         // softmax scale * log2(e)
+    int32_t debug_flags;
+};
+
+template <typename T>
+struct DTypeTraits;
+template <>
+struct DTypeTraits<__half> {
+    static constexpr int kFormat = 0;
+    __device__ static __forceinline__ uint32_t pack(float lo, float hi) {
+        __half2 v = __floats2half2_rn(lo, hi);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
+};
+template <>
+struct DTypeTraits<__nv_bfloat16> {
+    static constexpr int kFormat = 1;
+    __device__ static __forceinline__ uint32_t pack(float lo, float hi) {
+        __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
+};
+
+struct WaitCtl {
+    volatile int* abort;
+    int32_t* status;
+    int64_t timeout_ns;
+};
+
+// Wait for completion of phase `parity` of `bar`, for at most ctl.timeout_ns.
+// Returns false (after recording `err_bit` and raising the abort flag) on
+// expiry, or at once when another role has already aborted.
+__device__ __noinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, const WaitCtl& ctl, int err_bit,
+                                          bool honour_abort = true) {
+    const uint32_t addr = smem_u32(bar);
+    if (mbar_try_wait(addr, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    // iteration cap: ends the wait even if the global timer were not advancing
+    // (each outer round is 16 probes, well over 16 ns)
+    const int64_t max_rounds = ctl.timeout_ns / 16 + 1024;
+    for (int64_t round = 0;; ++round) {
+#pragma unroll 1
+        for (int i = 0; i < 16; ++i)
+            if (mbar_try_wait(addr, parity)) return true;
+        if (honour_abort && *ctl.abort) return false;
+        if (static_cast<int64_t>(globaltimer_ns() - t0) > ctl.timeout_ns || round > max_rounds) {
+            *ctl.abort = 1;
+            if (ctl.status) atomicOr(ctl.status, err_bit);
+            return false;
+        }
+    }
+}
+
+// All 32 lanes wait; the warp proceeds only if every lane saw the phase.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const WaitCtl& ctl, int err_bit) {
+    const bool ok = wait_bounded(bar, parity, ctl, err_bit);
+    return __all_sync(0xffffffffu, ok);
+}
+
+template <typename T, bool kRelBias>
+__device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint32_t tmem, const AttnParams& p,
+                                             const WaitCtl& ctl, int warp, int lane, int b, int h, int q_base,
+                                             int kv_end, int n_tiles, bool has_q1) {
+    const int wg = warp >> 2;                    // query tile of this warpgroup
+    const int row = ((warp & 3) << 5) + lane;    // row in tile == TMEM lane
+    const int i = q_base + wg * kBlockM + row;   // query index in the window
+    const int L = p.seq_len;
+    if (wg == 1 && !has_q1) return;
+
+    T* out_row = reinterpret_cast<T*>(p.out) + (static_cast<int64_t>(b) * L + i) * p.out_stride + h * kHeadDim;
+    if (n_tiles == 0) {  // no valid key: the context row is defined as zero
+        if (i < L) {
+            const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) reinterpret_cast<uint4*>(out_row)[c] = z;
+        }
+        return;
+    }
+
+    const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_addr + wg * kBlockN;
+    const uint32_t tO = tmem + lane_addr + kTmemO + wg * kHeadDim;
+    const float sl = p.scale_log2;
+    float* qrow = reinterpret_cast<float*>(smem + Smem::qr) + (wg * kBlockM + row) * kQrStride;
+    uint64_t* s_full = &bars[Smem::kSFull + wg];
+    uint64_t* p_full = &bars[Smem::kPFull + wg];
+
+    float qr_left = 0.f, qr_right = 0.f;
+    uint32_t s_parity = 0;
+    bool ok = true;
+    if constexpr (kRelBias) {
+        ok = warp_wait(s_full, s_parity, ctl, FDS_STATUS_TIMEOUT_SOFTMAX);
+        s_parity ^= 1;
+        if (ok) {
+            tc_fence_after();
+            uint32_t a[32], c2[32], d[16];
+            tmem_ld32(tS, a);
+            tmem_ld32(tS + 32, c2);
+            tmem_ld16(tS + 64, d);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) qrow[c] = __uint_as_float(a[c]) * sl;
+#pragma unroll
+            for (int c = 0; c < 32; ++c) qrow[32 + c] = __uint_as_float(c2[c]) * sl;
+#pragma unroll
+            for (int c = 0; c < kNumPos - 64; ++c) qrow[64 + c] = __uint_as_float(d[c]) * sl;
+            qr_left = __uint_as_float(a[0]) * sl;
+            qr_right = __uint_as_float(d[kNumPos - 1 - 64]) * sl;
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+    }
+
+    const int t0 = q_base + wg * kBlockM;  // first query row of this tile
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    for (int j = 0; ok && j < n_tiles; ++j) {
+        ok = warp_wait(s_full, s_parity, ctl, FDS_STATUS_TIMEOUT_SOFTMAX);
+        s_parity ^= 1;
+        if (!ok) break;
+        tc_fence_after();
+
+        uint32_t sr[128];
+        tmem_ld32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+        tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+        tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
+        tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
+        tmem_wait_ld();
+        float s[128];
+#pragma unroll
+        for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sr[c]);
+
+        const int n0 = j * kBlockN;
+        // tile class (uniform over the warpgroup): every pair left-saturated,
+        // every pair right-saturated, or near-diagonal (per-score gather)
+        const bool far_left = (n0 + kBlockN - 1) - t0 <= -kClampLeft;
+        const bool far_right = n0 - (t0 + kBlockM - 1) >= kClampRight;
+        const bool band = kRelBias && !far_left && !far_right;
+        if (band) {
+            const int d0 = n0 - i + kClampLeft;
+#pragma unroll
+            for (int c = 0; c < 128; ++c) {
+                const int idx = min(max(d0 + c, 0), kClampLeft + kClampRight);
+                s[c] = fmaf(s[c], sl, qrow[idx]);
+            }
+        }
+        if (n0 + kBlockN > kv_end) {
+            const int lim = kv_end - n0;
+#pragma unroll
+            for (int c = 0; c < 128; ++c)
+                if (c >= lim) s[c] = -INFINITY;
+        }
+        float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
+#pragma unroll
+        for (int c = 4; c < 128; c += 4) {
+            mx0 = fmaxf(mx0, s[c]);
+            mx1 = fmaxf(mx1, s[c + 1]);
+            mx2 = fmaxf(mx2, s[c + 2]);
+            mx3 = fmaxf(mx3, s[c + 3]);
+        }
+        const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+        float cb = 0.f;
+        if constexpr (kRelBias) cb = far_left ? qr_left : qr_right;
+        const float tile_max = band ? mx : fmaf(mx, sl, cb);
+
+        const bool rescale = tile_max > m_run + kRescaleThreshold;
+        float alpha = 1.f;
+        if (rescale) {
+            alpha = ex2_approx(m_run - tile_max);  // 0 on the first tile
+            m_run = tile_max;
+        }
+        const float mult = band ? 1.f : sl;
+        const float add = (band ? 0.f : cb) - m_run;
+        float ls0 = 0.f, ls1 = 0.f;
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                const float p0 = ex2_approx(fmaf(s[ch * 32 + 2 * c], mult, add));
+                const float p1 = ex2_approx(fmaf(s[ch * 32 + 2 * c + 1], mult, add));
+                ls0 += p0;
+                ls1 += p1;
+                pk[c] = DTypeTraits<T>::pack(p0, p1);
+            }
+            tmem_st16(tS + ch * 16, pk);
+        }
+        l_run = l_run * alpha + (ls0 + ls1);
+        if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+            // O is quiescent here: the commit that signalled this S tile also
+            // covered the previous P.V product, and the next one waits for P.
+            // (S is already consumed into P, so its registers are free.)
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                uint32_t o[32];
+                tmem_ld32(tO + 32 * half, o);
+                tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+                tmem_st32(tO + 32 * half, o);
+            }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(p_full);
+    }
+
+    if (!ok) return;
+    ok = warp_wait(&bars[Smem::kODone + wg], 0, ctl, FDS_STATUS_TIMEOUT_SOFTMAX);
+    if (!ok) return;
+    tc_fence_after();
+    uint32_t o[64];
+    tmem_ld32(tO, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+    tmem_ld32(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+    tmem_wait_ld();
+    if (i < L) {
+        const float inv = 1.f / l_run;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            uint4 v;
+            v.x = DTypeTraits<T>::pack(__uint_as_float(o[8 * c + 0]) * inv, __uint_as_float(o[8 * c + 1]) * inv);
+            v.y = DTypeTraits<T>::pack(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv);
+            v.z = DTypeTraits<T>::pack(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv);
+            v.w = DTypeTraits<T>::pack(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv);
+            reinterpret_cast<uint4*>(out_row)[c] = v;
+        }
+    }
+}
+
+template <typename T, bool kRelBias>
+__device__ __forceinline__ void mma_role(uint8_t* smem, uint64_t* bars, uint32_t tmem, const AttnParams& p,
+                                         const WaitCtl& ctl, int n_tiles, bool has_q1) {
+    constexpr int fmt = DTypeTraits<T>::kFormat;
+    constexpr uint32_t kIdescQK = idesc_f16(kBlockM, kBlockN, fmt, 0, 0);
+    constexpr uint32_t kIdescQR = idesc_f16(kBlockM, kRelRows, fmt, 0, 0);
+    constexpr uint32_t kIdescPV = idesc_f16(kBlockM, kHeadDim, fmt, 0, 1);
+    constexpr int err = FDS_STATUS_TIMEOUT_MMA;
+
+    bool ok = true;
+    if (p.debug_flags & FDS_DEBUG_FORCE_TIMEOUT) ok = wait_bounded(&bars[Smem::kNever], 0, ctl, err);
+    bool issued_any = false;
+
+    if (ok && n_tiles > 0) {
+        const int nq = has_q1 ? 2 : 1;
+        const uint64_t dq0 = sw128_desc(smem_u32(smem + Smem::q0));
+        const uint64_t dq1 = sw128_desc(smem_u32(smem + Smem::q1));
+        const uint32_t dk0 = smem_u32(smem + Smem::k);
+        const uint32_t dv0 = smem_u32(smem + Smem::v);
+        uint32_t p_parity = 0;  // bit w: next P phase of query tile w
+
+        ok = wait_bounded(&bars[Smem::kQ], 0, ctl, err);
+        if (ok) {
+            tc_fence_after();
+            issued_any = kRelBias;
+            if constexpr (kRelBias) {
+                const uint64_t dr = sw128_desc(smem_u32(smem + Smem::rel));
+                for (int w = 0; w < nq; ++w) {
+#pragma unroll
+                    for (int k = 0; k < kHeadDim / 16; ++k)
+                        mma_ss(tmem + w * kBlockN, (w ? dq1 : dq0) + 2 * k, dr + 2 * k, kIdescQR, k > 0);
+                    mma_commit(&bars[Smem::kSFull + w]);
+                }
+            }
+            ok = wait_bounded(&bars[Smem::kKFull + 0], 0, ctl, err);
+        }
+        // S(0) for each query tile (after its QR copy has left the S columns)
+        for (int w = 0; ok && w < nq; ++w) {
+            if constexpr (kRelBias) {
+                ok = wait_bounded(&bars[Smem::kPFull + w], (p_parity >> w) & 1, ctl, err);
+                p_parity ^= 1u << w;
+                if (!ok) break;
+            }
+            tc_fence_after();
+            issued_any = true;
+            const uint64_t dk = sw128_desc(dk0);
+#pragma unroll
+            for (int k = 0; k < kHeadDim / 16; ++k)
+                mma_ss(tmem + w * kBlockN, (w ? dq1 : dq0) + 2 * k, dk + 2 * k, kIdescQK, k > 0);
+            mma_commit(&bars[Smem::kSFull + w]);
+        }
+        for (int j = 0; ok && j < n_tiles; ++j) {
+            const int st = j % kStages;
+            ok = wait_bounded(&bars[Smem::kVFull + st], (j / kStages) & 1, ctl, err);
+            if (!ok) break;
+            const uint64_t dv = sw128_desc(dv0 + st * kTileBytes);
+            const bool more = j + 1 < n_tiles;
+            const int st1 = (j + 1) % kStages;
+            for (int w = 0; w < nq; ++w) {
+                ok = wait_bounded(&bars[Smem::kPFull + w], (p_parity >> w) & 1, ctl, err);
+                p_parity ^= 1u << w;
+                if (!ok) break;
+                tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < kBlockN / 16; ++k)
+                    mma_ts(tmem + kTmemO + w * kHeadDim, tmem + w * kBlockN + 8 * k, dv + 128 * k, kIdescPV,
+                           (j > 0 || k > 0) ? 1u : 0u);
+                if (w == nq - 1) mma_commit(&bars[Smem::kKvEmpty + st]);
+                if (more) {
+                    if (w == 0) {
+                        ok = wait_bounded(&bars[Smem::kKFull + st1], ((j + 1) / kStages) & 1, ctl, err);
+                        if (!ok) break;
+                        tc_fence_after();
+                    }
+                    const uint64_t dk = sw128_desc(dk0 + st1 * kTileBytes);
+#pragma unroll
+                    for (int k = 0; k < kHeadDim / 16; ++k)
+                        mma_ss(tmem + w * kBlockN, (w ? dq1 : dq0) + 2 * k, dk + 2 * k, kIdescQK, k > 0);
+                    mma_commit(&bars[Smem::kSFull + w]);
+                } else {
+                    mma_commit(&bars[Smem::kODone + w]);
+                }
+            }
+        }
+    }
+    // drain: every MMA issued above completes before TMEM is released
+    if (issued_any) {
+        mma_commit(&bars[Smem::kDrain]);
+        wait_bounded(&bars[Smem::kDrain], 0, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
+    }
+}
+
+template <bool kRelBias>
+__device__ __forceinline__ void load_role(uint8_t* smem, uint64_t* bars, const CUtensorMap* map_q,
+                                          const CUtensorMap* map_k, const CUtensorMap* map_v,
+                                          const CUtensorMap* map_r, const AttnParams& p, const WaitCtl& ctl,
+                                          int b, int h, int q_base, int n_tiles, bool has_q1) {
+    if (n_tiles == 0) return;
+    const uint32_t q_bytes = (has_q1 ? 2 : 1) * kTileBytes + (kRelBias ? kRelRows * 128 : 0);
+    mbar_arrive_expect_tx(&bars[Smem::kQ], q_bytes);
+    tma_load_3d(smem + Smem::q0, map_q, &bars[Smem::kQ], p.q_x0 + h * kHeadDim, q_base, b);
+    if (has_q1) tma_load_3d(smem + Smem::q1, map_q, &bars[Smem::kQ], p.q_x0 + h * kHeadDim, q_base + kBlockM, b);
+    if constexpr (kRelBias) tma_load_2d(smem + Smem::rel, map_r, &bars[Smem::kQ], 0, 0);
+
+    int issued_tiles = 0;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+        const int st = j % kStages;
+        if (j >= kStages) {
+            ok = wait_bounded(&bars[Smem::kKvEmpty + st], ((j / kStages) - 1) & 1, ctl, FDS_STATUS_TIMEOUT_LOAD);
+            if (!ok) break;
+        }
+        mbar_arrive_expect_tx(&bars[Smem::kKFull + st], kTileBytes);
+        tma_load_3d(smem + Smem::k + st * kTileBytes, map_k, &bars[Smem::kKFull + st], p.k_x0 + h * kHeadDim,
+                    j * kBlockN, b);
+        mbar_arrive_expect_tx(&bars[Smem::kVFull + st], kTileBytes);
+        tma_load_3d(smem + Smem::v + st * kTileBytes, map_v, &bars[Smem::kVFull + st], p.v_x0 + h * kHeadDim,
+                    j * kBlockN, b);
+        ++issued_tiles;
+    }
+    if (!ok) {
+        // aborted: let every copy already issued land before the CTA exits
+        wait_bounded(&bars[Smem::kQ], 0, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
+        for (int s = 0; s < kStages; ++s) {
+            // loads issued into stage s: tiles s, s + kStages, ... below issued_tiles
+            const int n = issued_tiles > s ? (issued_tiles - s + kStages - 1) / kStages : 0;
+            if (n == 0) continue;
+            wait_bounded(&bars[Smem::kKFull + s], (n - 1) & 1, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
+            wait_bounded(&bars[Smem::kVFull + s], (n - 1) & 1, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
+        }
+    }
+}
+
+template <typename T, bool kRelBias>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                    const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_r,
+                    const AttnParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Smem::bars);
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + Smem::misc);
+    int* abort_flag = reinterpret_cast<int*>(smem + Smem::misc + 4);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int b = blockIdx.y / p.heads;
+    const int h = blockIdx.y % p.heads;
+    const int q_base = blockIdx.x * kRowsPerCta;
+    const int L = p.seq_len;
+    const bool has_q1 = q_base + kBlockM < L;
+    int kv_end = L;
+    if (p.kv_len != nullptr) kv_end = min(max(p.kv_len[b], 0), L);
+    const int n_tiles = (kv_end + kBlockN - 1) / kBlockN;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bars[Smem::kQ], 1);
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&bars[Smem::kKFull + s], 1);
+            mbar_init(&bars[Smem::kVFull + s], 1);
+            mbar_init(&bars[Smem::kKvEmpty + s], 1);
+        }
+        for (int w = 0; w < 2; ++w) {
+            mbar_init(&bars[Smem::kSFull + w], 1);
+            mbar_init(&bars[Smem::kPFull + w], kBlockM);
+            mbar_init(&bars[Smem::kODone + w], 1);
+        }
+        mbar_init(&bars[Smem::kDrain], 1);
+        mbar_init(&bars[Smem::kNever], 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        fence_proxy_async_smem();
+    }
+    if (warp == kLoadWarp && lane == 0) {
+        prefetch_tensormap(&map_q);
+        prefetch_tensormap(&map_k);
+        prefetch_tensormap(&map_v);
+        if (kRelBias) prefetch_tensormap(&map_r);
+    }
+    if (warp == kMmaWarp) {
+        tmem_alloc(tmem_holder, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+    const WaitCtl ctl{abort_flag, p.status, p.timeout_ns > 0 ? p.timeout_ns : kDefaultTimeoutNs};
+
+    if (warp < kMmaWarp) {
+        softmax_role<T, kRelBias>(smem, bars, tmem, p, ctl, warp, lane, b, h, q_base, kv_end, n_tiles, has_q1);
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) mma_role<T, kRelBias>(smem, bars, tmem, p, ctl, n_tiles, has_q1);
+    } else {
+        if (lane == 0)
+            load_role<kRelBias>(smem, bars, &map_q, &map_k, &map_v, &map_r, p, ctl, b, h, q_base, n_tiles, has_q1);
+    }
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace fds

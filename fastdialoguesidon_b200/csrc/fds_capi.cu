@@ -1,0 +1,291 @@
+// fds_capi.cu - the extern "C" entry points declared in include/fds_b200.h:
+// argument checks, TMA tensor maps over the caller's buffers, and launches on
+// the caller's stream. No device allocation, no synchronisation, no host work
+// that depends on tensor contents (safe inside CUDA-graph stream capture).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "attn_kernel.cuh"
+#include "fds_b200.h"
+#include "rope.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int ok() {
+    g_last_error.clear();
+    return FDS_OK;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    });
+    return fn;
+}
+
+// Device must be compute capability 10.0 (B200 / sm_100a). Cached per device.
+int check_device() {
+    static int cached[64];  // 0 unknown, 1 ok, 2 unsupported
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= 64) return fail(FDS_ERR_UNSUPPORTED_DEVICE, "device index %d out of range", dev);
+    if (cached[dev] == 0) {
+        int major = 0, minor = 0;
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+        cached[dev] = (major == 10 && minor == 0) ? 1 : 2;
+    }
+    if (cached[dev] != 1)
+        return fail(FDS_ERR_UNSUPPORTED_DEVICE, "device %d is not sm_100 (B200); this library is built for sm_100a",
+                    dev);
+    return FDS_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 3-D map over a [batch, seq_len, width] view of rows with `row_stride` elements:
+// box = 64 columns x `box_rows` rows x 1 window, 128-byte swizzle, zero fill
+// past seq_len (so a tile never reads the next window's rows).
+int make_rows_map(CUtensorMap* map, const void* base, int dtype, int64_t width, int64_t seq_len, int64_t batch,
+                  int64_t row_stride, int box_rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (enc == nullptr) return fail(FDS_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled unavailable from the driver");
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(seq_len),
+                                static_cast<cuuint64_t>(batch)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_stride * 2),
+                                   static_cast<cuuint64_t>(row_stride * 2 * seq_len)};
+    const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUtensorMapDataType dt =
+        dtype == FDS_DTYPE_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(FDS_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return FDS_OK;
+}
+
+// 2-D map over the [73, 64] relative-key table, box 64 x 80 (rows 73..79 read as zero).
+int make_rel_map(CUtensorMap* map, const void* base, int dtype) {
+    EncodeTiledFn enc = encode_fn();
+    if (enc == nullptr) return fail(FDS_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled unavailable from the driver");
+    const cuuint64_t dims[2] = {64, fds::kNumPos};
+    const cuuint64_t strides[1] = {128};
+    const cuuint32_t box[2] = {64, fds::kRelRows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapDataType dt =
+        dtype == FDS_DTYPE_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(FDS_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled(rel) failed (%d)", static_cast<int>(r));
+    return FDS_OK;
+}
+
+template <typename T, bool kRelBias>
+int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mr,
+                const fds::AttnParams& p, int batch, cudaStream_t stream) {
+    auto kern = fds::attn_fwd_kernel<T, kRelBias>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fds::Smem::alloc);
+    if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    const dim3 grid((p.seq_len + fds::kRowsPerCta - 1) / fds::kRowsPerCta, batch * p.heads);
+    kern<<<grid, fds::kThreads, fds::Smem::alloc, stream>>>(mq, mk, mv, mr, p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
+    return FDS_OK;
+}
+
+int check_common(const void* qkv, int64_t qkv_row_stride, const void* out, int64_t out_row_stride, int batch,
+                 int heads, int seq_len, int head_dim, int dtype) {
+    if (qkv == nullptr || out == nullptr) return fail(FDS_ERR_INVALID_ARGUMENT, "null qkv/out pointer");
+    if (head_dim != 64) return fail(FDS_ERR_INVALID_ARGUMENT, "head_dim must be 64 (got %d)", head_dim);
+    if (dtype != FDS_DTYPE_FP16 && dtype != FDS_DTYPE_BF16)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "dtype must be FDS_DTYPE_FP16 or FDS_DTYPE_BF16 (got %d)", dtype);
+    if (batch < 1 || heads < 1 || seq_len < 1)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "batch, heads and seq_len must be >= 1 (got %d, %d, %d)", batch, heads,
+                    seq_len);
+    if (static_cast<int64_t>(batch) * heads > 65535)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "batch * heads must be <= 65535 (got %lld)",
+                    static_cast<long long>(batch) * heads);
+    const int64_t hid = static_cast<int64_t>(heads) * 64;
+    if (qkv_row_stride < 3 * hid)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "qkv row stride %lld < 3*heads*64 = %lld",
+                    static_cast<long long>(qkv_row_stride), static_cast<long long>(3 * hid));
+    if (qkv_row_stride % 8 != 0)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "qkv row stride must be a multiple of 8 elements (16 bytes)");
+    if (out_row_stride < hid)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "out row stride %lld < heads*64 = %lld",
+                    static_cast<long long>(out_row_stride), static_cast<long long>(hid));
+    if (out_row_stride % 8 != 0)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "out row stride must be a multiple of 8 elements (16 bytes)");
+    if (!aligned16(qkv) || !aligned16(out))
+        return fail(FDS_ERR_INVALID_ARGUMENT, "qkv and out must be 16-byte aligned");
+    return FDS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fds_abi_version(void) { return FDS_ABI_VERSION; }
+
+const char* fds_last_error(void) { return g_last_error.c_str(); }
+
+int fds_attn_smem_bytes(void) { return fds::Smem::alloc; }
+
+int fds_flexrel_attn_fwd(const FdsFlexRelArgs* a, void* stream) {
+    if (a == nullptr) return fail(FDS_ERR_INVALID_ARGUMENT, "null args");
+    int rc = check_common(a->qkv, a->qkv_row_stride, a->out, a->out_row_stride, a->batch, a->heads, a->seq_len,
+                          a->head_dim, a->dtype);
+    if (rc != FDS_OK) return rc;
+    if (a->rel == nullptr || !aligned16(a->rel))
+        return fail(FDS_ERR_INVALID_ARGUMENT, "rel must be a 16-byte aligned [73, 64] table");
+    if (!(a->scale > 0.f)) return fail(FDS_ERR_INVALID_ARGUMENT, "scale must be > 0");
+    if ((rc = check_device()) != FDS_OK) return rc;
+
+    CUtensorMap mqkv, mrel;
+    const int64_t hid = static_cast<int64_t>(a->heads) * 64;
+    if ((rc = make_rows_map(&mqkv, a->qkv, a->dtype, 3 * hid, a->seq_len, a->batch, a->qkv_row_stride,
+                            fds::kBlockM)) != FDS_OK)
+        return rc;
+    if ((rc = make_rel_map(&mrel, a->rel, a->dtype)) != FDS_OK) return rc;
+
+    fds::AttnParams p{};
+    p.out = a->out;
+    p.out_stride = a->out_row_stride;
+    p.kv_len = a->kv_len;
+    p.status = a->status;
+    p.timeout_ns = a->timeout_ns;
+    p.heads = a->heads;
+    p.seq_len = a->seq_len;
+    p.q_x0 = 0;
+    p.k_x0 = static_cast<int32_t>(hid);
+    p.v_x0 = static_cast<int32_t>(2 * hid);
+    p.scale_log2 = a->scale * 1.4426950408889634f;
+    p.debug_flags = a->debug_flags;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    rc = a->dtype == FDS_DTYPE_FP16 ? launch_attn<__half, true>(mqkv, mqkv, mqkv, mrel, p, a->batch, s)
+                                    : launch_attn<__nv_bfloat16, true>(mqkv, mqkv, mqkv, mrel, p, a->batch, s);
+    return rc == FDS_OK ? ok() : rc;
+}
+
+static int launch_rope(const void* qkv, int64_t qkv_row_stride, const float* cos_t, const float* sin_t, void* dq,
+                       void* dk, void* dv, int64_t dst_stride, int rows, int seq_len, int heads, int dtype,
+                       cudaStream_t s) {
+    const int parts = dv != nullptr ? 3 : 2;
+    const int64_t total = static_cast<int64_t>(rows) * heads * parts * 4;
+    const int threads = 256;
+    const int64_t blocks = (total + threads - 1) / threads;
+    if (blocks > 0x7fffffffLL) return fail(FDS_ERR_INVALID_ARGUMENT, "rope: too many rows");
+    if (dtype == FDS_DTYPE_FP16)
+        fds::rope_rotate_kernel<__half><<<static_cast<unsigned>(blocks), threads, 0, s>>>(
+            static_cast<const __half*>(qkv), qkv_row_stride, cos_t, sin_t, static_cast<__half*>(dq),
+            static_cast<__half*>(dk), static_cast<__half*>(dv), dst_stride, rows, seq_len, heads);
+    else
+        fds::rope_rotate_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), threads, 0, s>>>(
+            static_cast<const __nv_bfloat16*>(qkv), qkv_row_stride, cos_t, sin_t, static_cast<__nv_bfloat16*>(dq),
+            static_cast<__nv_bfloat16*>(dk), static_cast<__nv_bfloat16*>(dv), dst_stride, rows, seq_len, heads);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "rope launch: %s", cudaGetErrorString(e));
+    return FDS_OK;
+}
+
+int fds_rope_attn_fwd(const FdsRopeArgs* a, void* stream) {
+    if (a == nullptr) return fail(FDS_ERR_INVALID_ARGUMENT, "null args");
+    int rc = check_common(a->qkv, a->qkv_row_stride, a->out, a->out_row_stride, a->batch, a->heads, a->seq_len,
+                          a->head_dim, a->dtype);
+    if (rc != FDS_OK) return rc;
+    if (a->cos == nullptr || a->sin == nullptr || !aligned16(a->cos) || !aligned16(a->sin))
+        return fail(FDS_ERR_INVALID_ARGUMENT, "cos/sin must be 16-byte aligned fp32 [>= seq_len, 64] tables");
+    if (a->qk_scratch == nullptr || !aligned16(a->qk_scratch))
+        return fail(FDS_ERR_INVALID_ARGUMENT, "qk_scratch must be a 16-byte aligned [batch*seq_len, 2*heads*64] buffer");
+    if (!(a->scale > 0.f)) return fail(FDS_ERR_INVALID_ARGUMENT, "scale must be > 0");
+    if ((rc = check_device()) != FDS_OK) return rc;
+
+    const int64_t hid = static_cast<int64_t>(a->heads) * 64;
+    const int64_t rows = static_cast<int64_t>(a->batch) * a->seq_len;
+    if (rows > 0x7fffffffLL) return fail(FDS_ERR_INVALID_ARGUMENT, "batch*seq_len too large");
+    CUtensorMap mqk, mv;
+    if ((rc = make_rows_map(&mqk, a->qk_scratch, a->dtype, 2 * hid, a->seq_len, a->batch, 2 * hid, fds::kBlockM)) !=
+        FDS_OK)
+        return rc;
+    if ((rc = make_rows_map(&mv, a->qkv, a->dtype, 3 * hid, a->seq_len, a->batch, a->qkv_row_stride, fds::kBlockM)) !=
+        FDS_OK)
+        return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    char* scratch = static_cast<char*>(a->qk_scratch);
+    rc = launch_rope(a->qkv, a->qkv_row_stride, a->cos, a->sin, scratch, scratch + hid * 2, nullptr, 2 * hid,
+                     static_cast<int>(rows), a->seq_len, a->heads, a->dtype, s);
+    if (rc != FDS_OK) return rc;
+
+    fds::AttnParams p{};
+    p.out = a->out;
+    p.out_stride = a->out_row_stride;
+    p.kv_len = nullptr;
+    p.status = a->status;
+    p.timeout_ns = a->timeout_ns;
+    p.heads = a->heads;
+    p.seq_len = a->seq_len;
+    p.q_x0 = 0;
+    p.k_x0 = static_cast<int32_t>(hid);
+    p.v_x0 = static_cast<int32_t>(2 * hid);
+    p.scale_log2 = a->scale * 1.4426950408889634f;
+    p.debug_flags = a->debug_flags;
+    rc = a->dtype == FDS_DTYPE_FP16 ? launch_attn<__half, false>(mqk, mqk, mv, mqk, p, a->batch, s)
+                                    : launch_attn<__nv_bfloat16, false>(mqk, mqk, mv, mqk, p, a->batch, s);
+    return rc == FDS_OK ? ok() : rc;
+}
+
+int fds_rope_split(const void* qkv, int64_t qkv_row_stride, const float* cos_t, const float* sin_t, void* out,
+                   int32_t rows, int32_t seq_len, int32_t heads, int32_t head_dim, int32_t dtype, void* stream) {
+    if (qkv == nullptr || out == nullptr || cos_t == nullptr || sin_t == nullptr)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "null pointer");
+    if (head_dim != 64) return fail(FDS_ERR_INVALID_ARGUMENT, "head_dim must be 64 (got %d)", head_dim);
+    if (dtype != FDS_DTYPE_FP16 && dtype != FDS_DTYPE_BF16)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "dtype must be FDS_DTYPE_FP16 or FDS_DTYPE_BF16");
+    if (rows < 0 || seq_len < 1 || heads < 1)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "rows >= 0, seq_len >= 1, heads >= 1 required");
+    const int64_t hid = static_cast<int64_t>(heads) * 64;
+    if (qkv_row_stride < 3 * hid || qkv_row_stride % 8 != 0)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "qkv row stride must be >= 3*heads*64 and a multiple of 8");
+    if (!aligned16(qkv) || !aligned16(out) || !aligned16(cos_t) || !aligned16(sin_t))
+        return fail(FDS_ERR_INVALID_ARGUMENT, "all buffers must be 16-byte aligned");
+    if (rows == 0) return ok();
+    int rc = check_device();
+    if (rc != FDS_OK) return rc;
+    char* o = static_cast<char*>(out);
+    const int64_t plane = static_cast<int64_t>(rows) * hid * 2;
+    rc = launch_rope(qkv, qkv_row_stride, cos_t, sin_t, o, o + plane, o + 2 * plane, hid, rows, seq_len, heads, dtype,
+                     static_cast<cudaStream_t>(stream));
+    return rc == FDS_OK ? ok() : rc;
+}
+
+}  // extern "C"

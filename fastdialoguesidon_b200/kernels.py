@@ -1,0 +1,253 @@
+"""Attention ops of the FastDialogueSidon hot path on B200 (sm_100a).
+
+Drop-in for the attention half of ``triton/src/fds_triton/kernels.py``: the
+same names, argument order, layouts, dtypes and "``out`` written in place when
+given" contract, computed by the hand-written tcgen05 kernels behind the C ABI
+in ``include/fds_b200.h``. There is one encoder kernel (no fused/split
+dispatch), no autotuning, no host synchronisation and no allocation other than
+``out`` (and the DiT's rotated-q|k scratch), so every call is safe inside
+``torch.cuda.graph`` capture once the device has run one eager call.
+
+Errors: invalid arguments raise :class:`FdsError` before any launch. It
+subclasses both ``AssertionError`` (what the reference's ``assert`` checks
+raise, ``kernels.py:430, 641``) and ``RuntimeError``. A missing native library
+or a non-CUDA tensor raises as well: there is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _native as N
+
+LEFT, RIGHT = 64, 8          # kernels.py:298 clamp of j - i
+NUM_POS = LEFT + RIGHT + 1   # 73 relative-key table rows
+NUM_POS_PAD = 128            # kept for API parity with kernels.py:300
+LOG2E = 1.4426950408889634
+HEAD_DIM = 64
+
+
+class FdsError(AssertionError, RuntimeError):
+    """Invalid argument or failed launch of an FDS kernel."""
+
+
+_DTYPES = {torch.float16: N.FDS_DTYPE_FP16, torch.bfloat16: N.FDS_DTYPE_BF16}
+_status_words: dict[int, torch.Tensor] = {}
+
+
+def _check(cond: bool, msg: str) -> None:
+    if not cond:
+        raise FdsError(msg)
+
+
+def _status(device: torch.device) -> torch.Tensor:
+    """Per-device int32 word the kernels OR their bounded-wait error bits into."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    st = _status_words.get(idx)
+    if st is None:
+        st = torch.zeros(4, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status_words[idx] = st
+    return st
+
+
+def check_status(device: torch.device | int | None = None, clear: bool = True) -> int:
+    """Synchronise ``device`` and raise :class:`FdsError` if any kernel on it
+    recorded an expired bounded wait since the last check. Returns the bits."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       (device if isinstance(device, int) else device.index))
+    st = _status(dev)
+    torch.cuda.synchronize(dev)
+    bits = int(st[0].item())
+    if clear and bits:
+        st.zero_()
+    if bits:
+        raise FdsError(f"FDS kernel on {dev} reported a bounded-wait timeout (status bits 0x{bits:x})")
+    return bits
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _rows_operand(t: torch.Tensor, name: str) -> None:
+    _check(isinstance(t, torch.Tensor), f"{name} must be a torch.Tensor")
+    _check(t.is_cuda, f"{name} must be a CUDA tensor (no CPU fallback)")
+    _check(t.dim() == 2, f"{name} must be 2-D [rows, columns], got {tuple(t.shape)}")
+    _check(t.dtype in _DTYPES, f"{name} must be float16 or bfloat16, got {t.dtype}")
+    _check(t.stride(1) == 1, f"{name} columns must be contiguous (stride(1) == 1)")
+    _check(t.shape[0] <= 1 or t.stride(0) % 8 == 0, f"{name} row stride must be a multiple of 8 elements")
+    _check(t.data_ptr() % 16 == 0, f"{name} must be 16-byte aligned")
+
+
+def _raise_rc(rc: int, what: str) -> None:
+    if rc != N.FDS_OK:
+        raise FdsError(f"{what} failed (code {rc}): {N.last_error()}")
+
+
+def flexrel_attention(qkv: torch.Tensor, batch: int, heads: int, rel: torch.Tensor,
+                      out: torch.Tensor | None = None, kv_len: torch.Tensor | None = None,
+                      *, timeout_ns: int = 0, debug_flags: int = 0) -> torch.Tensor:
+    """Relative-key self-attention of one w2v-BERT layer.
+
+    qkv [B*L, 3*H*64] fp16/bf16 (q | k | v column blocks, rows b*L + t),
+    rel [73, 64] same dtype -> context [B*L, H*64] (qkv dtype), written into
+    ``out`` when given. ``kv_len`` (int32 CUDA [B], optional) excludes keys
+    t >= kv_len[b] -- the key-padding mask of a bucketed batch; every query row
+    (padded ones included) attends over the valid keys, as with HF's additive
+    mask. A window with kv_len 0 yields zeros.
+
+    Same contract as the reference ``flexrel_attention``
+    (triton/src/fds_triton/kernels.py:422-442); ``kv_len`` is an addition.
+    """
+    _rows_operand(qkv, "qkv")
+    rows, width = qkv.shape
+    _check(batch >= 1 and heads >= 1, "batch and heads must be >= 1")
+    _check(width % 3 == 0, f"qkv width {width} is not 3 * hidden")
+    hidden = width // 3
+    _check(hidden % heads == 0, f"hidden {hidden} not divisible by heads {heads}")
+    dim = hidden // heads
+    _check(dim == HEAD_DIM, f"head_dim must be 64, got {dim}")
+    _check(rows % batch == 0 and rows > 0, f"rows {rows} not a positive multiple of batch {batch}")
+    length = rows // batch
+    _check(isinstance(rel, torch.Tensor) and rel.shape == (NUM_POS, dim) and rel.is_contiguous(),
+           f"rel must be a contiguous [{NUM_POS}, {dim}] tensor")
+    _check(rel.dtype == qkv.dtype and rel.device == qkv.device, "rel must match qkv's dtype and device")
+    _check(rel.data_ptr() % 16 == 0, "rel must be 16-byte aligned")
+    if out is None:
+        out = torch.empty(rows, hidden, device=qkv.device, dtype=qkv.dtype)
+    else:
+        _rows_operand(out, "out")
+        _check(out.shape == (rows, hidden), f"out must be [{rows}, {hidden}], got {tuple(out.shape)}")
+        _check(out.dtype == qkv.dtype and out.device == qkv.device, "out must match qkv's dtype and device")
+    kv_ptr = None
+    if kv_len is not None:
+        _check(isinstance(kv_len, torch.Tensor) and kv_len.is_cuda and kv_len.dtype == torch.int32
+               and kv_len.shape == (batch,) and kv_len.is_contiguous() and kv_len.device == qkv.device,
+               f"kv_len must be a contiguous int32 CUDA tensor of shape [{batch}] on qkv's device")
+        kv_ptr = kv_len.data_ptr()
+    dev = qkv.device
+    lib = N.load()
+    with torch.cuda.device(dev):
+        args = N.FdsFlexRelArgs(
+            qkv=qkv.data_ptr(), qkv_row_stride=qkv.stride(0) if rows > 1 else width,
+            rel=rel.data_ptr(), out=out.data_ptr(),
+            out_row_stride=out.stride(0) if rows > 1 else hidden,
+            kv_len=kv_ptr, status=_status(dev).data_ptr(),
+            batch=batch, heads=heads, seq_len=length, head_dim=dim, dtype=_DTYPES[qkv.dtype],
+            scale=1.0 / math.sqrt(dim), timeout_ns=int(timeout_ns), debug_flags=int(debug_flags),
+        )
+        rc = lib.fds_flexrel_attn_fwd(ctypes.byref(args), _stream_ptr(dev))
+    _raise_rc(rc, "fds_flexrel_attn_fwd")
+    return out
+
+
+def flexrel_attention_split(qkv: torch.Tensor, batch: int, heads: int, rel: torch.Tensor,
+                            out: torch.Tensor | None = None) -> torch.Tensor:
+    """Same contract and result as :func:`flexrel_attention`
+    (reference ``kernels.py:634``). The reference splits the work into two cuDNN
+    causal passes plus a band merge; on B200 one kernel does all of it."""
+    return flexrel_attention(qkv, batch, heads, rel, out)
+
+
+def cudnn_attention_available(device=None) -> bool:
+    """Kept for ``model.py:89``; the B200 path needs no cuDNN, so this only
+    reports whether the device can run these kernels (sm_100)."""
+    return torch.cuda.is_available() and torch.cuda.get_device_capability(device) == (10, 0)
+
+
+def encoder_attention(qkv, batch, heads, rel, impl: str = "split", kv_len=None):
+    """Reference ``kernels.py:674``; ``impl`` ("split" / "fused" / "auto") is
+    accepted and ignored: there is a single kernel."""
+    _check(impl in ("split", "fused", "auto"), f"unknown impl {impl!r}")
+    return flexrel_attention(qkv, batch, heads, rel, kv_len=kv_len)
+
+
+def _rope_tables(cos: torch.Tensor, sin: torch.Tensor, length: int, ref: torch.Tensor) -> None:
+    for name, t in (("cos", cos), ("sin", sin)):
+        _check(isinstance(t, torch.Tensor) and t.dtype == torch.float32 and t.dim() == 2
+               and t.shape[1] == HEAD_DIM and t.shape[0] >= length and t.is_contiguous()
+               and t.device == ref.device and t.data_ptr() % 16 == 0,
+               f"{name} must be a contiguous fp32 [>= {length}, 64] table on {ref.device}")
+
+
+def rope_split(qkv: torch.Tensor, length: int, heads: int, cos: torch.Tensor,
+               sin: torch.Tensor) -> torch.Tensor:
+    """qkv [B*L, 3*HID] -> [3, B*L, HID]: rotated q, rotated k, v (bit-exact),
+    position = row % length. Reference ``kernels.py:476-487``."""
+    _rows_operand(qkv, "qkv")
+    rows, width = qkv.shape
+    _check(width % 3 == 0, "qkv width is not 3 * hidden")
+    hid = width // 3
+    _check(hid % heads == 0 and hid // heads == HEAD_DIM, "head_dim must be 64")
+    _check(length >= 1, "length must be >= 1")
+    _rope_tables(cos, sin, min(length, rows) if rows else 1, qkv)
+    out = torch.empty(3, rows, hid, device=qkv.device, dtype=qkv.dtype)
+    lib = N.load()
+    with torch.cuda.device(qkv.device):
+        rc = lib.fds_rope_split(qkv.data_ptr(), qkv.stride(0) if rows > 1 else width, cos.data_ptr(),
+                                sin.data_ptr(), out.data_ptr(), rows, length, heads, HEAD_DIM,
+                                _DTYPES[qkv.dtype], _stream_ptr(qkv.device))
+    _raise_rc(rc, "fds_rope_split")
+    return out
+
+
+def rope_attention(qkv: torch.Tensor, batch: int, heads: int, cos: torch.Tensor, sin: torch.Tensor,
+                   out: torch.Tensor | None = None, scratch: torch.Tensor | None = None,
+                   *, timeout_ns: int = 0, debug_flags: int = 0) -> torch.Tensor:
+    """DiT head self-attention: RoPE on q and k (frame index t = row % L), then
+    bidirectional softmax(q k^T / 8) v. qkv [B*L, 3*HID] -> [B*L, HID].
+
+    Replaces ``K.rope_split`` + ``F.scaled_dot_product_attention`` at
+    triton/src/fds_triton/model.py:319-325. ``scratch`` ([B*L, 2*HID], qkv
+    dtype) receives the rotated q | k; it is allocated when not given.
+    """
+    _rows_operand(qkv, "qkv")
+    rows, width = qkv.shape
+    _check(batch >= 1 and heads >= 1, "batch and heads must be >= 1")
+    _check(width % 3 == 0, "qkv width is not 3 * hidden")
+    hid = width // 3
+    _check(hid % heads == 0 and hid // heads == HEAD_DIM, "head_dim must be 64")
+    _check(rows % batch == 0 and rows > 0, f"rows {rows} not a positive multiple of batch {batch}")
+    length = rows // batch
+    _rope_tables(cos, sin, length, qkv)
+    if out is None:
+        out = torch.empty(rows, hid, device=qkv.device, dtype=qkv.dtype)
+    else:
+        _rows_operand(out, "out")
+        _check(out.shape == (rows, hid) and out.dtype == qkv.dtype and out.device == qkv.device,
+               f"out must be a [{rows}, {hid}] {qkv.dtype} tensor on {qkv.device}")
+    if scratch is None:
+        scratch = torch.empty(rows, 2 * hid, device=qkv.device, dtype=qkv.dtype)
+    else:
+        _check(scratch.shape == (rows, 2 * hid) and scratch.is_contiguous() and scratch.dtype == qkv.dtype
+               and scratch.device == qkv.device and scratch.data_ptr() % 16 == 0,
+               f"scratch must be a contiguous [{rows}, {2 * hid}] {qkv.dtype} tensor on {qkv.device}")
+    dev = qkv.device
+    lib = N.load()
+    with torch.cuda.device(dev):
+        args = N.FdsRopeArgs(
+            qkv=qkv.data_ptr(), qkv_row_stride=qkv.stride(0) if rows > 1 else width,
+            cos=cos.data_ptr(), sin=sin.data_ptr(), qk_scratch=scratch.data_ptr(), out=out.data_ptr(),
+            out_row_stride=out.stride(0) if rows > 1 else hid, status=_status(dev).data_ptr(),
+            batch=batch, heads=heads, seq_len=length, head_dim=HEAD_DIM, dtype=_DTYPES[qkv.dtype],
+            scale=1.0 / math.sqrt(HEAD_DIM), timeout_ns=int(timeout_ns), debug_flags=int(debug_flags),
+        )
+        rc = lib.fds_rope_attn_fwd(ctypes.byref(args), _stream_ptr(dev))
+    _raise_rc(rc, "fds_rope_attn_fwd")
+    return out
+
+
+def rope_tables(max_seq: int, device=None, dim: int = HEAD_DIM, base: float = 10000.0):
+    """fp32 cos/sin [max_seq, dim] tables as the reference builds them
+    (model.py:201-205: inv_freq = base^(-arange(0, dim/2)/(dim/2)), cat([f, f]))."""
+    half = dim // 2
+    inv_freq = 1.0 / (base ** (torch.arange(0, half, dtype=torch.float32) / float(half)))
+    freqs = torch.outer(torch.arange(max_seq, dtype=torch.float32), inv_freq)
+    cos = torch.cat([freqs.cos(), freqs.cos()], -1).contiguous()
+    sin = torch.cat([freqs.sin(), freqs.sin()], -1).contiguous()
+    if device is not None:
+        cos, sin = cos.to(device), sin.to(device)
+    return cos, sin

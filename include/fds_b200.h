@@ -1,0 +1,134 @@
+/*
+ * fds_b200.h - C ABI of the B200 (sm_100a) attention hot path of FastDialogueSidon.
+ *
+ * Plain C: device pointers, sizes and a stream handle (a cudaStream_t passed as
+ * void*), no torch or C++ types, so that ctypes / cffi / any FFI can bind it.
+ * Every entry point launches on the given stream, never synchronises, never
+ * allocates device memory, and returns FDS_OK or an error code before any
+ * launch when an argument is invalid (fds_last_error() then holds a message).
+ *
+ * Numerics: fp16 or bf16 operands, fp32 accumulation, fp32 online softmax in
+ * log2 units, P rounded to the operand type for the P.V product (the same
+ * rounding points as the reference's Triton kernels).
+ */
+#ifndef FDS_B200_H
+#define FDS_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FDS_ABI_VERSION 1
+
+#if defined(_WIN32)
+#define FDS_API __declspec(dllexport)
+#else
+#define FDS_API __attribute__((visibility("default")))
+#endif
+
+/* return codes */
+#define FDS_OK 0
+#define FDS_ERR_INVALID_ARGUMENT 1
+#define FDS_ERR_UNSUPPORTED_DEVICE 2
+#define FDS_ERR_CUDA 3
+#define FDS_ERR_TENSOR_MAP 4
+
+/* operand types */
+#define FDS_DTYPE_FP16 0
+#define FDS_DTYPE_BF16 1
+
+/* bits written (atomicOr) into *status by a kernel whose bounded wait expired */
+#define FDS_STATUS_TIMEOUT_LOAD 0x1    /* TMA producer waited too long for a free stage */
+#define FDS_STATUS_TIMEOUT_MMA 0x2     /* MMA issuer waited too long for operands / P */
+#define FDS_STATUS_TIMEOUT_SOFTMAX 0x4 /* softmax warps waited too long for S / O */
+#define FDS_STATUS_TIMEOUT_DRAIN 0x8   /* in-flight copies or MMAs did not drain at exit */
+
+/* debug flags (tests only): make the MMA issuer wait on a barrier that nothing
+ * arrives on, so that the bounded-wait error path runs without a real hang. */
+#define FDS_DEBUG_FORCE_TIMEOUT 0x1
+
+/*
+ * Encoder relative_key self-attention (w2v-BERT conformer layer):
+ *   S[b,h,i,j] = (q_i . k_j + q_i . rel[clamp(j - i, -64, +8) + 64]) * scale
+ *   O[b,i,h,:] = softmax_j(S[b,h,i,:]) . V        over keys j < kv_len[b]
+ * qkv is [batch*seq_len, >= 3*heads*64] row-major, q | k | v column blocks at
+ * column offsets 0, heads*64, 2*heads*64 (the fused QKV GEMM output).
+ * Replaces: triton/src/fds_triton/kernels.py:422 flexrel_attention (and the
+ * equivalent split path kernels.py:634 flexrel_attention_split).
+ */
+typedef struct FdsFlexRelArgs {
+    const void* qkv;          /* device, dtype, [batch*seq_len, qkv_row_stride] */
+    int64_t qkv_row_stride;   /* elements; multiple of 8, >= 3*heads*64 */
+    const void* rel;          /* device, dtype, [73, 64] contiguous */
+    void* out;                /* device, dtype, [batch*seq_len, out_row_stride] */
+    int64_t out_row_stride;   /* elements; >= heads*64 */
+    const int32_t* kv_len;    /* device [batch] valid key count per window, or NULL (= seq_len) */
+    int32_t* status;          /* device word for bounded-wait errors, or NULL */
+    int32_t batch;
+    int32_t heads;
+    int32_t seq_len;
+    int32_t head_dim;         /* must be 64 */
+    int32_t dtype;            /* FDS_DTYPE_* */
+    float scale;              /* softmax scale on (qk + qr); the reference uses 1/sqrt(64) */
+    int64_t timeout_ns;       /* bound on every in-kernel wait; <= 0 selects 2 s */
+    int32_t debug_flags;      /* 0 in production */
+} FdsFlexRelArgs;
+
+FDS_API int fds_flexrel_attn_fwd(const FdsFlexRelArgs* args, void* stream);
+
+/*
+ * DiT head RoPE self-attention (bidirectional, no bias, no mask):
+ *   q' = q*cos[t] + rotate_half(q)*sin[t], k' likewise (rotate_half(x) = [-x2, x1]),
+ *   O = softmax(q' k'^T * scale) V
+ * cos/sin are fp32 tables [>= seq_len, 64] indexed by the frame index t.
+ * qk_scratch receives the rotated q | k rows ([batch*seq_len, 2*heads*64], dtype):
+ * K is reused by every query tile, so it is rotated once per call rather than
+ * once per tile.
+ * Replaces: triton/src/fds_triton/model.py:319-325 (kernels.py:476 rope_split +
+ * F.scaled_dot_product_attention).
+ */
+typedef struct FdsRopeArgs {
+    const void* qkv;          /* device, dtype, [batch*seq_len, qkv_row_stride] */
+    int64_t qkv_row_stride;   /* elements; multiple of 8, >= 3*heads*64 */
+    const float* cos;         /* device fp32 [>= seq_len, 64] contiguous */
+    const float* sin;         /* device fp32 [>= seq_len, 64] contiguous */
+    void* qk_scratch;         /* device, dtype, [batch*seq_len, 2*heads*64] contiguous */
+    void* out;                /* device, dtype, [batch*seq_len, out_row_stride] */
+    int64_t out_row_stride;   /* elements; >= heads*64 */
+    int32_t* status;          /* device word for bounded-wait errors, or NULL */
+    int32_t batch;
+    int32_t heads;
+    int32_t seq_len;
+    int32_t head_dim;         /* must be 64 */
+    int32_t dtype;            /* FDS_DTYPE_* */
+    float scale;              /* the reference uses 1/sqrt(64) (SDPA default) */
+    int64_t timeout_ns;
+    int32_t debug_flags;
+} FdsRopeArgs;
+
+FDS_API int fds_rope_attn_fwd(const FdsRopeArgs* args, void* stream);
+
+/*
+ * RoPE split: out[0] = rot(q), out[1] = rot(k), out[2] = v as [3, batch*seq_len, heads*64].
+ * Replaces: triton/src/fds_triton/kernels.py:476 rope_split (pos = token % seq_len).
+ */
+FDS_API int fds_rope_split(const void* qkv, int64_t qkv_row_stride, const float* cos, const float* sin,
+                   void* out, int32_t rows, int32_t seq_len, int32_t heads, int32_t head_dim,
+                   int32_t dtype, void* stream);
+
+/* Version of this ABI (FDS_ABI_VERSION). */
+FDS_API int fds_abi_version(void);
+
+/* Message for the last error returned on this host thread ("" if none). */
+FDS_API const char* fds_last_error(void);
+
+/* Shared-memory bytes a CTA of the attention kernels requests (for diagnostics). */
+FDS_API int fds_attn_smem_bytes(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FDS_B200_H */

@@ -1,0 +1,179 @@
+"""Encoder relative_key attention on the B200 vs the CPU oracle and the
+reference-generated golden fixtures.
+
+Tolerance: max-abs <= 2e-3 vs the fp32 reference on the
+same inputs and SNR >= 55 dB, for fp16 operands. bf16 cases use the
+reference's own test threshold (SNR > 40 dB, triton/tests/test_kernels.py:119).
+"""
+
+import pytest
+import torch
+
+import fastdialoguesidon_b200 as F
+from fastdialoguesidon_b200 import _native as N
+from oracle import flexrel_oracle as O
+from conftest import golden_names, load_golden
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-3
+MIN_SNR = 55.0
+BF16_MIN_SNR = 40.0
+
+
+def _check(exp: torch.Tensor, got: torch.Tensor, dtype=torch.float16):
+    got = got.float().cpu()
+    snr = O.snr_db(exp, got)
+    if dtype == torch.bfloat16:
+        assert snr > BF16_MIN_SNR, snr
+        return
+    err = O.max_abs(exp, got)
+    assert err <= MAX_ABS and snr >= MIN_SNR, (err, snr)
+
+
+def _inputs(batch, length, heads, seed, dtype=torch.float16, std=1.0, rel_std=1.0):
+    gen = torch.Generator().manual_seed(seed)
+    qkv = (torch.randn(batch * length, 3 * heads * 64, generator=gen) * std).to(dtype)
+    rel = (torch.randn(73, 64, generator=gen) * rel_std).to(dtype)
+    return qkv, rel
+
+
+@pytest.mark.parametrize("name", golden_names("core_"))
+def test_golden_fixture(cuda_device, name):
+    g = load_golden(name)
+    m = g["meta"]
+    qkv = torch.from_numpy(g["qkv"]).to(cuda_device)
+    rel = torch.from_numpy(g["rel"]).to(cuda_device)
+    kv = torch.from_numpy(g["kv_len"]).to(cuda_device) if "kv_len" in g else None
+    out = F.flexrel_attention(qkv, m["batch"], m["heads"], rel, kv_len=kv)
+    F.check_status()
+    _check(torch.from_numpy(g["expected"]), out)
+
+
+@pytest.mark.parametrize("B,L", [(1, 500), (2, 333), (1, 160)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_reference_shapes(cuda_device, B, L, dtype):
+    """The reference's kernel-test shapes (test_kernels.py:112-129), H=16, N(0,1)."""
+    qkv, rel = _inputs(B, L, 16, seed=0, dtype=dtype)
+    exp = O.flexrel_attention(qkv, B, 16, rel)
+    out = F.flexrel_attention(qkv.to(cuda_device), B, 16, rel.to(cuda_device))
+    split = F.flexrel_attention_split(qkv.to(cuda_device), B, 16, rel.to(cuda_device))
+    F.check_status()
+    _check(exp, out, dtype)
+    assert torch.equal(out, split)
+
+
+@pytest.mark.parametrize("L", [1, 2, 7, 63, 64, 72, 73, 127, 128, 129, 200, 255, 256, 257, 383, 384, 385, 640, 1000])
+def test_edge_lengths(cuda_device, L):
+    qkv, rel = _inputs(2, L, 2, seed=L)
+    exp = O.flexrel_attention(qkv, 2, 2, rel)
+    out = F.flexrel_attention(qkv.to(cuda_device), 2, 2, rel.to(cuda_device))
+    F.check_status()
+    _check(exp, out)
+
+
+def test_config2_layer_full_size(cuda_device):
+    """BASELINE config 2 shape for one layer: L=6000, 16 x 64 heads; q/k/v with
+    the spread of x ~ N(0,1) projected by W ~ N(0, 0.02) (std 0.64), rel ~ N(0, 0.02)."""
+    qkv, rel = _inputs(1, 6000, 16, seed=11, std=0.64, rel_std=0.02)
+    exp = O.flexrel_attention(qkv, 1, 16, rel)
+    out = F.flexrel_attention(qkv.to(cuda_device), 1, 16, rel.to(cuda_device))
+    F.check_status()
+    _check(exp, out)
+
+
+def test_full_size_peaky(cuda_device):
+    """L=6000 with N(0,1) operands (sharp softmax, frequent running-max updates), 4 heads."""
+    qkv, rel = _inputs(1, 6000, 4, seed=12)
+    exp = O.flexrel_attention(qkv, 1, 4, rel)
+    out = F.flexrel_attention(qkv.to(cuda_device), 1, 4, rel.to(cuda_device))
+    F.check_status()
+    _check(exp, out)
+
+
+def test_config3_variable_windows(cuda_device):
+    """BASELINE config 3 shape: 8 windows U(3.2, 120) s, bucketed to 500 frames,
+    key-padding via kv_len (2 heads: heads are independent)."""
+    gen = torch.Generator().manual_seed(3)
+    secs = torch.rand(8, generator=gen) * (120 - 3.2) + 3.2
+    frames = torch.ceil(secs * 50).to(torch.int32)
+    buckets = ((frames + 499) // 500) * 500
+    L = int(buckets.max())
+    qkv, rel = _inputs(8, L, 2, seed=13, std=0.64, rel_std=0.02)
+    exp = O.flexrel_attention(qkv, 8, 2, rel, kv_len=frames)
+    out = F.flexrel_attention(qkv.to(cuda_device), 8, 2, rel.to(cuda_device), kv_len=frames.to(cuda_device))
+    F.check_status()
+    _check(exp, out)
+
+
+def test_kv_len_edges(cuda_device):
+    """kv_len 0 (zeros), 1, a tile boundary, L and beyond L (clamped)."""
+    L = 300
+    kv = torch.tensor([0, 1, 128, 129, L, L + 50], dtype=torch.int32)
+    qkv, rel = _inputs(6, L, 2, seed=21)
+    exp = O.flexrel_attention(qkv, 6, 2, rel, kv_len=kv)
+    out = F.flexrel_attention(qkv.to(cuda_device), 6, 2, rel.to(cuda_device), kv_len=kv.to(cuda_device))
+    F.check_status()
+    _check(exp, out)
+    assert torch.count_nonzero(out[:L]) == 0
+
+
+def test_strided_in_place(cuda_device):
+    """qkv as a column slice of a wider buffer; out written in place into a strided view."""
+    B, L, H = 2, 257, 4
+    qkv, rel = _inputs(B, L, H, seed=31)
+    wide = torch.zeros(B * L, 3 * H * 64 + 64, dtype=torch.float16)
+    wide[:, 32:32 + 3 * H * 64] = qkv
+    wide = wide.to(cuda_device)
+    big = torch.full((B * L, H * 64 + 128), 7.0, dtype=torch.float16, device=cuda_device)
+    view = big[:, 64:64 + H * 64]
+    ret = F.flexrel_attention(wide[:, 32:32 + 3 * H * 64], B, H, rel.to(cuda_device), out=view)
+    F.check_status()
+    assert ret.data_ptr() == view.data_ptr()
+    _check(O.flexrel_attention(qkv, B, H, rel), view)
+    assert torch.all(big[:, :64] == 7.0) and torch.all(big[:, 64 + H * 64:] == 7.0)
+
+
+def test_deterministic_and_graph_capture(cuda_device):
+    B, L, H = 1, 1000, 16
+    qkv, rel = _inputs(B, L, H, seed=41)
+    qkv, rel = qkv.to(cuda_device), rel.to(cuda_device)
+    eager = F.flexrel_attention(qkv, B, H, rel)
+    again = F.flexrel_attention(qkv, B, H, rel)
+    assert torch.equal(eager, again)
+    out = torch.empty_like(eager)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        F.flexrel_attention(qkv, B, H, rel, out=out)  # warm-up on the capture stream
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    out.zero_()
+    with torch.cuda.graph(g):
+        F.flexrel_attention(qkv, B, H, rel, out=out)
+    g.replay()
+    torch.cuda.synchronize()
+    F.check_status()
+    assert torch.equal(out, eager)
+
+
+def test_torch_op(cuda_device):
+    qkv, rel = _inputs(1, 160, 16, seed=51)
+    qkv, rel = qkv.to(cuda_device), rel.to(cuda_device)
+    a = torch.ops.fds.flexrel_attention(qkv, 1, 16, rel)
+    b = F.flexrel_attention(qkv, 1, 16, rel)
+    assert torch.equal(a, b)
+
+
+def test_bounded_wait_reports_and_recovers(cuda_device):
+    """A wait on a barrier that nothing arrives on expires after 2 ms: the kernel
+    records the MMA-timeout bit and exits; the context stays usable."""
+    qkv, rel = _inputs(1, 300, 2, seed=61)
+    qkv, rel = qkv.to(cuda_device), rel.to(cuda_device)
+    F.flexrel_attention(qkv, 1, 2, rel, timeout_ns=2_000_000, debug_flags=N.FDS_DEBUG_FORCE_TIMEOUT)
+    with pytest.raises(F.FdsError, match="timeout"):
+        F.check_status()
+    assert F.check_status() == 0  # cleared
+    out = F.flexrel_attention(qkv, 1, 2, rel)
+    F.check_status()
+    _check(O.flexrel_attention(qkv.cpu(), 1, 2, rel.cpu()), out)
