@@ -1,0 +1,473 @@
+"""Benchmark of the FastDialogueSidon attention hot path on B200.
+
+Headline (BASELINE.json metric, configs[1]): the 13-layer w2v-BERT encoder
+relative_key attention of one 120 s window (L=6000, 16 x 64 heads, fp16
+operands, fp32 softmax/accumulation), in ms per window (lower is better).
+
+One step = the 13 layer calls of one window, each on its own precomputed QKV
+(13 x 36.9 MB = 479 MB of inputs > the 126 MB L2, so no flush is needed
+between steps). The QKV of layer i follows the stacking rule: x_{i+1} =
+x_i + Attn_i(x_i) W_out^T on an fp32 residual, x_0 ~ N(0,1), weights
+~ N(0, 0.02), rel ~ N(0, 0.02) (random init, seeded per window).
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Multi-GPU: launched under torch.distributed.run, one process per GPU; every
+rank owns whole windows (weak scaling, no data-path collective); the step time
+is the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+L_WINDOW = 6000          # 120 s at 50 Hz
+ENC_LAYERS, ENC_HEADS = 13, 16
+DIT_LAYERS, DIT_HEADS = 8, 12
+HEAD_DIM = 64
+FLOP_ENC_LAYER = 4 * ENC_HEADS * L_WINDOW * L_WINDOW * HEAD_DIM   # 147.456 GFLOP (QK^T + PV)
+FLOP_DIT_LAYER = 4 * DIT_HEADS * L_WINDOW * L_WINDOW * HEAD_DIM   # 110.592 GFLOP
+DATASHEET_DENSE_FP16_TFLOPS = 2250.0
+FALLBACK_PEAK_TFLOPS = 1590.0
+METRIC = "ms per 120 s window (13-layer rel-bias attn)"
+UNIT = "ms/window"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-dit", action="store_true")
+    ap.add_argument("--case", choices=("enc1", "dit1"), default=None,
+                    help="profiling case: W + K eager launches of one layer (encoder or DiT) at L=6000")
+    return ap.parse_args()
+
+
+def config_dict(n_gpus: int) -> dict:
+    return {
+        "workload": "config2: 13-layer encoder relative_key attention, one 120 s window",
+        "seq_len": L_WINDOW, "heads": ENC_HEADS, "head_dim": HEAD_DIM, "layers": ENC_LAYERS,
+        "windows_per_gpu_per_step": 1, "global_batch": n_gpus,
+        "parallelism": f"windows partitioned over {n_gpus} GPU(s), no collectives",
+        "l2": "inputs 479 MB per step > 126 MB L2 (no flush)",
+        "timing": "13 calls captured in one CUDA graph per step; CUDA events on the launch stream",
+    }
+
+
+def measured_peak():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops"]), "of measured (cuBLAS bf16 burst, MEASURED_PEAKS.json)"
+    return FALLBACK_PEAK_TFLOPS, "of fallback (1.59 PFLOP/s bf16, earlier measurement on this pool)"
+
+
+def ncu_traffic():
+    """dram bytes per launch of the encoder kernel from the committed ncu summary."""
+    p = REPO / "profiles" / "ncu_traffic.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("flexrel_l6000_bytes_per_launch")
+    return None
+
+
+# ------------------------------------------------------------------ clocks
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks / throttle reasons while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.rows: list[list[str]] = []
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            self.gpu = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:  # noqa: BLE001
+            self.gpu = None
+
+    def __enter__(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"]
+        if self.gpu:
+            cmd[1:1] = ["-i", self.gpu]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        loaded = [r for r in self.rows if len(r) >= 9 and r[3].isdigit() and int(r[3]) > 0]
+        use = loaded or [r for r in self.rows if len(r) >= 9]
+        if not use:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [float(r[0]) for r in use if r[0].replace(".", "").isdigit()]
+        reasons = sorted({names[k] for r in use for k in range(4) if r[5 + k].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(use[0][1]) if use[0][1].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(use),
+                "power_w_max": max(float(r[2]) for r in use if r[2].replace(".", "").isdigit())}
+
+
+# ------------------------------------------------------------------ workload
+
+
+def make_window(seed: int, device: torch.device, layers: int = ENC_LAYERS, length: int = L_WINDOW,
+                heads: int = ENC_HEADS):
+    """Per-layer fp16 QKV [L, 3*H*64] and rel [73, 64] for one window, stacked
+    on an fp32 residual through this library's attention (setup, untimed)."""
+    import fastdialoguesidon_b200 as F
+
+    hidden = heads * HEAD_DIM
+    gen = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(length, hidden, generator=gen, device=device)
+    qkvs, rels = [], []
+    for _ in range(layers):
+        w_qkv = torch.randn(3 * hidden, hidden, generator=gen, device=device) * 0.02
+        w_out = torch.randn(hidden, hidden, generator=gen, device=device) * 0.02
+        rel = (torch.randn(73, HEAD_DIM, generator=gen, device=device) * 0.02).half()
+        qkv = (x @ w_qkv.t()).half()
+        ctx = F.flexrel_attention(qkv, 1, heads, rel)
+        x = x + ctx.float() @ w_out.t()
+        qkvs.append(qkv)
+        rels.append(rel)
+    F.check_status(device)
+    return qkvs, rels
+
+
+def time_graph(fn, steps: int, warmup: int, device: torch.device, dist_on: bool) -> float:
+    """Capture fn() once; W untimed replays; K timed replays between barrier +
+    synchronize on both sides; returns elapsed ms (CUDA events on the replay stream)."""
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream(device).wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize(device)
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        g.replay()
+    end.record(stream)
+    torch.cuda.synchronize(device)
+    if dist_on:
+        torch.distributed.barrier()
+    ms = start.elapsed_time(end)
+    del g
+    return ms
+
+
+def e2e_encoder(qkvs, rels, steps: int, warmup: int, device: torch.device, dist_on: bool):
+    """The same metric through the public API with host buffers: every step copies
+    its 13 QKV + rel tables host->device (pinned) and the 13 contexts back,
+    overlapped over a copy-in / compute / copy-out stream pipeline."""
+    import fastdialoguesidon_b200 as F
+
+    host_in = [q.cpu().pin_memory() for q in qkvs]
+    host_rel = [r.cpu().pin_memory() for r in rels]
+    host_out = [torch.empty(q.shape[0], q.shape[1] // 3, dtype=q.dtype).pin_memory() for q in qkvs]
+    dev_in = [torch.empty_like(q) for q in qkvs]
+    dev_rel = [torch.empty_like(r) for r in rels]
+    dev_out = [torch.empty(q.shape[0], q.shape[1] // 3, dtype=q.dtype, device=device) for q in qkvs]
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    comp = torch.cuda.current_stream(device)
+    n = len(qkvs)
+    h2d = sum(t.numel() * t.element_size() for t in host_in + host_rel)
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+    ev_in = [torch.cuda.Event() for _ in range(n)]
+    ev_c = [torch.cuda.Event() for _ in range(n)]
+    ev_out = [torch.cuda.Event() for _ in range(n)]
+
+    def step():
+        for i in range(n):
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(ev_c[i])  # the previous step's layer i is done with dev_in[i]
+                dev_in[i].copy_(host_in[i], non_blocking=True)
+                dev_rel[i].copy_(host_rel[i], non_blocking=True)
+                ev_in[i].record(s_in)
+            comp.wait_event(ev_in[i])
+            comp.wait_event(ev_out[i])  # dev_out[i] read back by the previous step
+            F.flexrel_attention(dev_in[i], 1, ENC_HEADS, dev_rel[i], out=dev_out[i])
+            ev_c[i].record(comp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_c[i])
+                host_out[i].copy_(dev_out[i], non_blocking=True)
+                ev_out[i].record(s_out)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(device)
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(s_in)
+    for _ in range(steps):
+        step()
+    s_out.wait_stream(comp)
+    end.record(s_out)
+    torch.cuda.synchronize(device)
+    if dist_on:
+        torch.distributed.barrier()
+    F.check_status(device)
+    return start.elapsed_time(end), h2d, d2h
+
+
+_CPU_INPUTS = None
+
+
+def _cpu_inputs():
+    global _CPU_INPUTS
+    if _CPU_INPUTS is None:
+        gen = torch.Generator().manual_seed(0)
+        shape = (1, ENC_HEADS, L_WINDOW, HEAD_DIM)
+        q, k, v = (torch.randn(shape, generator=gen) * 0.64 for _ in range(3))
+        rel = torch.randn(73, HEAD_DIM, generator=gen) * 0.02
+        _CPU_INPUTS = (q, k, v, rel)
+    return _CPU_INPUTS
+
+
+def cpu_sample_ms_per_window(rows: int = 6000, threads: int | None = None) -> tuple[float, dict]:
+    """The oracle (fp32 torch, chunked like the reference's torch_core_chunked,
+    trt/src/fastdialoguesidon/flexrel_triton.py:298-329) on the host cores: the
+    first ``rows`` query rows of one layer of one window against all 6000 keys,
+    scaled to 13 layers x 6000 rows."""
+    from oracle import flexrel_oracle as O
+
+    if threads:
+        torch.set_num_threads(threads)
+    q, k, v, rel = _cpu_inputs()
+    L = L_WINDOW
+    t0 = time.perf_counter()
+    for start in range(0, rows, 512):
+        stop = min(start + 512, rows)
+        O.flexrel_rows(q, k, v, rel, start, stop)
+    dt = time.perf_counter() - t0
+    ms = dt * 1e3 * (L / rows) * ENC_LAYERS
+    return ms, {"cores": torch.get_num_threads(), "cpu_count": os.cpu_count(),
+                "sample": f"oracle fp32 core, {rows} query rows x 16 heads x 6000 keys of one layer "
+                          f"({dt:.2f} s), scaled x{L / rows:.2f} rows x 13 layers"}
+
+
+# ------------------------------------------------------------------ arms
+
+
+def run_reference(args, rank: int) -> None:
+    """CPU arm: the oracle port of the reference's fp32 path on all host cores,
+    each step a 128-row sample of one layer scaled to a whole window."""
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    rows = 128
+    for _ in range(max(args.warmup, 1)):
+        cpu_sample_ms_per_window(rows)
+    vals = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        ms, info = cpu_sample_ms_per_window(rows)
+        vals.append(ms)
+        if time.perf_counter() - t0 > 150:  # keep the arm within a few minutes
+            break
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": len(vals), "warmup": args.warmup, "ms_per_step": round(value, 3),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,0.64) q/k/v, N(0,0.02) rel)", "config": config_dict(args.gpus),
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": info["sample"] + "; median over steps"},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank: int, world: int, local_rank: int) -> None:
+    import fastdialoguesidon_b200 as F
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dist_on = world > 1
+    if dist_on:
+        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    qkvs, rels = make_window(seed=1000 + rank, device=device)
+    outs = [torch.empty(L_WINDOW, ENC_HEADS * HEAD_DIM, dtype=torch.float16, device=device) for _ in qkvs]
+
+    def enc_step():
+        for q, r, o in zip(qkvs, rels, outs):
+            F.flexrel_attention(q, 1, ENC_HEADS, r, out=o)
+
+    with ClockSampler(device) as clocks:
+        ms = time_graph(enc_step, args.steps, args.warmup, device, dist_on)
+    F.check_status(device)
+    e2e_steps = max(3, min(args.steps, 60))
+    e2e_ms, h2d, d2h = e2e_encoder(qkvs, rels, e2e_steps, max(3, min(args.warmup, 5)), device, dist_on)
+
+    dit = None
+    if not args.no_dit:
+        dq = []
+        gen = torch.Generator(device=device).manual_seed(2000 + rank)
+        for _ in range(DIT_LAYERS):
+            dq.append((torch.randn(L_WINDOW, 3 * DIT_HEADS * HEAD_DIM, generator=gen, device=device)
+                       * 0.55).half())
+        cos, sin = F.rope_tables(L_WINDOW, device)
+        dout = [torch.empty(L_WINDOW, DIT_HEADS * HEAD_DIM, dtype=torch.float16, device=device) for _ in dq]
+        scratch = torch.empty(L_WINDOW, 2 * DIT_HEADS * HEAD_DIM, dtype=torch.float16, device=device)
+
+        def dit_step():
+            for q, o in zip(dq, dout):
+                F.rope_attention(q, 1, DIT_HEADS, cos, sin, out=o, scratch=scratch)
+
+        dsteps = max(3, args.steps // 2)
+        dms = time_graph(dit_step, dsteps, args.warmup, device, dist_on)
+        F.check_status(device)
+        dit = (dms, dsteps)
+
+    t = torch.tensor([ms, e2e_ms, dit[0] if dit else 0.0], dtype=torch.float64, device=device)
+    if dist_on:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms, e2e_ms, dms = (float(x) for x in t.tolist())
+
+    if rank == 0:
+        K = args.steps
+        windows = K * world
+        value = ms / windows                      # whole-job ms per window
+        per_launch_ms = ms / (K * ENC_LAYERS)     # each GPU runs its launches back to back
+        achieved = FLOP_ENC_LAYER / (per_launch_ms * 1e-3) / 1e12
+        peak, peak_note = measured_peak()
+        traffic = ncu_traffic()
+        line = {
+            "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": round(ms / K, 4), "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic (seeded random-init weights / inputs of the config-2 shapes)",
+            "config": config_dict(world),
+            "tflops": round(FLOP_ENC_LAYER * ENC_LAYERS * windows / (ms * 1e-3) / 1e12, 1),
+            "pct_dense_fp16_peak": round(100 * achieved / DATASHEET_DENSE_FP16_TFLOPS, 1),
+            "windows_per_s": round(windows / (ms * 1e-3), 2),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "kernel": "fds::attn_fwd_kernel<__half, true> (one encoder layer, 147.456 GFLOP)",
+                         "peak_note": peak_note},
+            "e2e": {"value": round(e2e_ms / (e2e_steps * world), 4), "unit": UNIT,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "note": "public API flexrel_attention, pinned host QKV/rel in, context out, per step"},
+            "gpu_launches": K * ENC_LAYERS,
+            "clocks": clocks.summary(),
+        }
+        if dit:
+            dsteps = dit[1]
+            dper = dms / (dsteps * DIT_LAYERS)
+            line["dit"] = {"workload": "config4: 8-layer DiT RoPE attention, L=6000, 12 x 64 heads",
+                           "ms_per_window": round(dms / dsteps, 4),
+                           "tflops": round(FLOP_DIT_LAYER / (dper * 1e-3) / 1e12, 1),
+                           "steps": dsteps, "launches_per_window": 2 * DIT_LAYERS}
+        if world == 1 and not args.no_cpu_baseline:
+            cms, info = cpu_sample_ms_per_window(rows=1024, threads=os.cpu_count())
+            line["cpu_baseline"] = {"value": round(cms, 1), "unit": UNIT, "cores": info["cores"],
+                                    "kind": "port", "sample": info["sample"]}
+        print(json.dumps(line), flush=True)
+
+    if dist_on:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def run_case(args) -> None:
+    """Small profiling case for ncu: one layer's kernel, W + K eager launches."""
+    import fastdialoguesidon_b200 as F
+
+    device = torch.device("cuda", 0)
+    gen = torch.Generator(device=device).manual_seed(7)
+    if args.case == "enc1":
+        qkv = (torch.randn(L_WINDOW, 3 * ENC_HEADS * HEAD_DIM, generator=gen, device=device) * 0.64).half()
+        rel = (torch.randn(73, HEAD_DIM, generator=gen, device=device) * 0.02).half()
+        out = torch.empty(L_WINDOW, ENC_HEADS * HEAD_DIM, dtype=torch.float16, device=device)
+        fn, flop = (lambda: F.flexrel_attention(qkv, 1, ENC_HEADS, rel, out=out)), FLOP_ENC_LAYER
+    else:
+        qkv = (torch.randn(L_WINDOW, 3 * DIT_HEADS * HEAD_DIM, generator=gen, device=device) * 0.55).half()
+        cos, sin = F.rope_tables(L_WINDOW, device)
+        out = torch.empty(L_WINDOW, DIT_HEADS * HEAD_DIM, dtype=torch.float16, device=device)
+        scratch = torch.empty(L_WINDOW, 2 * DIT_HEADS * HEAD_DIM, dtype=torch.float16, device=device)
+        fn, flop = (lambda: F.rope_attention(qkv, 1, DIT_HEADS, cos, sin, out=out, scratch=scratch)), FLOP_DIT_LAYER
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        fn()
+    end.record()
+    torch.cuda.synchronize(device)
+    F.check_status(device)
+    ms = start.elapsed_time(end) / max(args.steps, 1)
+    print(json.dumps({"case": args.case, "ms_per_launch": round(ms, 4),
+                      "tflops": round(flop / (ms * 1e-3) / 1e12, 1)}), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.case:
+        run_case(args)
+        return
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world == 1 and args.gpus > 1:
+        raise SystemExit("for --gpus > 1 launch under torch.distributed.run (one process per GPU)")
+    run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -24,6 +24,14 @@ INCLUDE_DIR = REPO_DIR / "include"
 SOURCES = ["fds_capi.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
+# The attention kernels split their register file with setmaxnreg
+# (csrc/attn_kernel.cuh: 2 x 128 threads at 232 + 128 threads at 40). That
+# split assumes the CTA is launched with exactly this many registers per
+# thread; a different count could make the increase wait forever, so the build
+# refuses to produce a library in that case.
+ATTN_KERNEL_MARK = "attn_fwd_kernel"
+ATTN_LAUNCH_REGS = 168
+
 
 def nvcc_path() -> str:
     cand = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
@@ -53,22 +61,40 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     LIB_DIR.mkdir(parents=True, exist_ok=True)
     tmp = LIB_PATH.with_suffix(".so.tmp")
     cmd = [
-        nvcc_path(), *ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17",
+        nvcc_path(), *ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", "-Xptxas=-v",
         "-Xcompiler", "-fPIC,-fvisibility=hidden", "-shared",
         "-I", str(INCLUDE_DIR),
         "-o", str(tmp),
         *[str(CSRC / s) for s in SOURCES],
     ]
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), flush=True)
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
     if verbose:
         sys.stdout.write(res.stdout + res.stderr)
+    check_launch_registers(res.stdout + res.stderr)
     os.replace(tmp, LIB_PATH)
     return LIB_PATH
+
+
+def check_launch_registers(ptxas_log: str) -> None:
+    """Every attention kernel entry must report ATTN_LAUNCH_REGS registers."""
+    current, seen = None, 0
+    for line in ptxas_log.splitlines():
+        if "Compiling entry function" in line:
+            current = line
+        elif current and "Used" in line and "registers" in line:
+            if ATTN_KERNEL_MARK in current:
+                regs = int(line.split("Used")[1].split("registers")[0])
+                if regs != ATTN_LAUNCH_REGS:
+                    raise RuntimeError(f"attention kernel launches with {regs} registers per thread, expected "
+                                       f"{ATTN_LAUNCH_REGS} (the setmaxnreg split depends on it): {current}")
+                seen += 1
+            current = None
+    if seen == 0:
+        raise RuntimeError("no attention kernel found in the ptxas report")
 
 
 if __name__ == "__main__":

@@ -1,14 +1,22 @@
 // attn_kernel.cuh - sm_100a attention forward with an optional relative_key bias.
 //
 // One CTA owns 256 query rows of one (window, head): two 128-row query tiles
-// (Q0, Q1) that share every K/V tile. Warp roles (320 threads):
+// (Q0, Q1) that share every K/V tile. Warp roles (384 threads, 3 warpgroups):
 //   warps 0-3  softmax for Q0 (thread = query row = TMEM lane)
 //   warps 4-7  softmax for Q1
-//   warp  8    MMA issuer (one thread) and TMEM owner
-//   warp  9    TMA producer (one thread)
-// TMEM (512 columns): S0 [0,128)  S1 [128,256)  O0 [256,320)  O1 [320,384).
-// P (the exponentiated scores, 16-bit) overwrites the first 64 columns of its
-// S tile and feeds the P.V product straight from TMEM.
+//   warp  8    MMA issuer (whole warp runs the schedule, one elected lane
+//              issues each group of tcgen05.mma) and TMEM owner
+//   warp  9    TMA producer (same convention)
+//   warps 10-11 idle (complete the third warpgroup)
+// Registers: launched at 168 per thread; the third warpgroup gives back down
+// to 56 and the two softmax warpgroups take 224 (256*224 + 128*56 = 384*168),
+// enough to hold a row of S (128 fp32) and of P (64 packed pairs) at once.
+// TMEM (512 columns): S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384)
+//                     O0 [384,448) O1 [448,512).
+// P (the exponentiated scores, two 16-bit values per column) has its own
+// columns, so S(j+1) = Q K(j+1)^T is issued as soon as the softmax warps have
+// pulled S(j) into registers and runs under their exponentials, and
+// P(j) V(j) runs under the next tile's softmax.
 //
 // Relative bias (encoder): bias(i, j) = q_i . rel[clamp(j - i, -64, 8) + 64].
 // Per query tile the MMA computes QR = Q . rel^T (N = 80, rows 73..79 zero)
@@ -54,9 +62,15 @@ constexpr int kRelRows = 80;       // table rows padded to a multiple of 16 (MMA
 constexpr int kQrStride = 74;      // floats per row of the shared QR copy (conflict-free gather)
 constexpr int kMmaWarp = 8;
 constexpr int kLoadWarp = 9;
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
+constexpr int kLaunchRegs = 168;     // per thread at launch (checked at build time)
+constexpr int kSoftmaxRegs = 232;
+constexpr int kControlRegs = 40;
+static_assert(256 * kSoftmaxRegs + 128 * kControlRegs <= kThreads * kLaunchRegs, "register split exceeds the launch pool");
 constexpr int kTmemCols = 512;
-constexpr int kTmemO = 256;        // first O column
+constexpr int kTmemS = 0;          // S_w at kTmemS + 128 w
+constexpr int kTmemP = 256;        // P_w at kTmemP + 64 w
+constexpr int kTmemO = 384;        // O_w at kTmemO + 64 w
 constexpr float kRescaleThreshold = 8.0f;
 constexpr int64_t kDefaultTimeoutNs = 2000000000LL;
 
@@ -72,11 +86,13 @@ struct Smem {
     static constexpr int kQ = 0;
     static constexpr int kKFull = 1;
     static constexpr int kVFull = kKFull + kStages;
-    static constexpr int kKvEmpty = kVFull + kStages;
-    static constexpr int kSFull = kKvEmpty + kStages;
-    static constexpr int kPFull = kSFull + 2;
-    static constexpr int kODone = kPFull + 2;
-    static constexpr int kDrain = kODone + 2;
+    static constexpr int kKEmpty = kVFull + kStages;    // MMA -> producer: K stage consumed
+    static constexpr int kVEmpty = kKEmpty + kStages;   // MMA -> producer: V stage consumed
+    static constexpr int kSFull = kVEmpty + kStages;    // MMA -> softmax: S(j) (or QR) in TMEM
+    static constexpr int kSFree = kSFull + 2;           // softmax -> MMA: S(j) read into registers
+    static constexpr int kPFull = kSFree + 2;           // softmax -> MMA: P(j) in TMEM, O rescaled
+    static constexpr int kPvDone = kPFull + 2;          // MMA -> softmax: P(j) V(j) complete
+    static constexpr int kDrain = kPvDone + 2;
     static constexpr int kNever = kDrain + 1;
     static constexpr int kNumBars = kNever + 1;
     static constexpr int misc = bars + kNumBars * 8;
@@ -127,7 +143,7 @@ struct WaitCtl {
 // Wait for completion of phase `parity` of `bar`, for at most ctl.timeout_ns.
 // Returns false (after recording `err_bit` and raising the abort flag) on
 // expiry, or at once when another role has already aborted.
-__device__ __noinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, const WaitCtl& ctl, int err_bit,
+__device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, const WaitCtl& ctl, int err_bit,
                                           bool honour_abort = true) {
     const uint32_t addr = smem_u32(bar);
     if (mbar_try_wait(addr, parity)) return true;
@@ -154,6 +170,14 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const 
     return __all_sync(0xffffffffu, ok);
 }
 
+// Arrive once per warp on `bar` (initialised with count 4 for a warpgroup):
+// every lane's prior tcgen05 traffic is ordered before the arrival.
+__device__ __forceinline__ void warp_arrive(uint64_t* bar, int lane) {
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar);
+}
+
 template <typename T, bool kRelBias>
 __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint32_t tmem, const AttnParams& p,
                                              const WaitCtl& ctl, int warp, int lane, int b, int h, int q_base,
@@ -175,12 +199,15 @@ __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint
     }
 
     const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tS = tmem + lane_addr + wg * kBlockN;
+    const uint32_t tS = tmem + lane_addr + kTmemS + wg * kBlockN;
+    const uint32_t tP = tmem + lane_addr + kTmemP + wg * (kBlockN / 2);
     const uint32_t tO = tmem + lane_addr + kTmemO + wg * kHeadDim;
     const float sl = p.scale_log2;
     float* qrow = reinterpret_cast<float*>(smem + Smem::qr) + (wg * kBlockM + row) * kQrStride;
     uint64_t* s_full = &bars[Smem::kSFull + wg];
+    uint64_t* s_free = &bars[Smem::kSFree + wg];
     uint64_t* p_full = &bars[Smem::kPFull + wg];
+    uint64_t* pv_done = &bars[Smem::kPvDone + wg];
 
     float qr_left = 0.f, qr_right = 0.f;
     uint32_t s_parity = 0;
@@ -195,6 +222,7 @@ __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint
             tmem_ld32(tS + 32, c2);
             tmem_ld16(tS + 64, d);
             tmem_wait_ld();
+            warp_arrive(s_free, lane);  // the S columns may now receive S(0)
 #pragma unroll
             for (int c = 0; c < 32; ++c) qrow[c] = __uint_as_float(a[c]) * sl;
 #pragma unroll
@@ -203,8 +231,6 @@ __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint
             for (int c = 0; c < kNumPos - 64; ++c) qrow[64 + c] = __uint_as_float(d[c]) * sl;
             qr_left = __uint_as_float(a[0]) * sl;
             qr_right = __uint_as_float(d[kNumPos - 1 - 64]) * sl;
-            tc_fence_before();
-            mbar_arrive(p_full);
         }
     }
 
@@ -223,6 +249,7 @@ __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint
         tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
         tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
         tmem_wait_ld();
+        warp_arrive(s_free, lane);  // the MMA may now compute S(j+1) into these columns
         float s[128];
 #pragma unroll
         for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sr[c]);
@@ -247,18 +274,18 @@ __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint
             for (int c = 0; c < 128; ++c)
                 if (c >= lim) s[c] = -INFINITY;
         }
-        float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
+        float mx[8];
 #pragma unroll
-        for (int c = 4; c < 128; c += 4) {
-            mx0 = fmaxf(mx0, s[c]);
-            mx1 = fmaxf(mx1, s[c + 1]);
-            mx2 = fmaxf(mx2, s[c + 2]);
-            mx3 = fmaxf(mx3, s[c + 3]);
+        for (int u = 0; u < 8; ++u) mx[u] = s[u];
+#pragma unroll
+        for (int c = 8; c < 128; c += 16) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) mx[u] = fmax3(mx[u], s[c + u], s[c + 8 + u]);
         }
-        const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+        const float mxa = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
         float cb = 0.f;
         if constexpr (kRelBias) cb = far_left ? qr_left : qr_right;
-        const float tile_max = band ? mx : fmaf(mx, sl, cb);
+        const float tile_max = band ? mxa : fmaf(mxa, sl, cb);
 
         const bool rescale = tile_max > m_run + kRescaleThreshold;
         float alpha = 1.f;
@@ -268,25 +295,38 @@ __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint
         }
         const float mult = band ? 1.f : sl;
         const float add = (band ? 0.f : cb) - m_run;
-        float ls0 = 0.f, ls1 = 0.f;
+
+        // exponentials into packed 16-bit pairs, held in registers; 2 of every
+        // 5 pairs go through the FMA-pipe polynomial so that the MUFU and FMA
+        // pipes carry similar loads
+        uint32_t pk[64];
+        float2 ls[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        const float2 mult2 = make_float2(mult, mult), add2 = make_float2(add, add);
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-            uint32_t pk[16];
-#pragma unroll
-            for (int c = 0; c < 16; ++c) {
-                const float p0 = ex2_approx(fmaf(s[ch * 32 + 2 * c], mult, add));
-                const float p1 = ex2_approx(fmaf(s[ch * 32 + 2 * c + 1], mult, add));
-                ls0 += p0;
-                ls1 += p1;
-                pk[c] = DTypeTraits<T>::pack(p0, p1);
+        for (int c = 0; c < 64; ++c) {
+            const float2 x = ffma2(make_float2(s[2 * c], s[2 * c + 1]), mult2, add2);
+            float2 pp;
+            if (c % 5 == 1 || c % 5 == 3) {
+                pp = exp2_poly2(x);
+            } else {
+                pp.x = ex2_approx(x.x);
+                pp.y = ex2_approx(x.y);
             }
-            tmem_st16(tS + ch * 16, pk);
+            ls[c & 1] = fadd2(ls[c & 1], pp);
+            pk[c] = DTypeTraits<T>::pack(pp.x, pp.y);
         }
-        l_run = l_run * alpha + (ls0 + ls1);
+        l_run = l_run * alpha + ((ls[0].x + ls[0].y) + (ls[1].x + ls[1].y));
+
+        if (j > 0) {
+            // P(j-1) V(j-1) must be complete before its P columns are rewritten
+            // and before O is rescaled (its latency hides under the work above).
+            ok = warp_wait(pv_done, (j - 1) & 1, ctl, FDS_STATUS_TIMEOUT_SOFTMAX);
+            if (!ok) break;
+            tc_fence_after();
+        }
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) tmem_st16(tP + ch * 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[ch * 16]));
         if (j > 0 && __any_sync(0xffffffffu, rescale)) {
-            // O is quiescent here: the commit that signalled this S tile also
-            // covered the previous P.V product, and the next one waits for P.
-            // (S is already consumed into P, so its registers are free.)
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 uint32_t o[32];
@@ -298,12 +338,11 @@ __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint
             }
         }
         tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(p_full);
+        warp_arrive(p_full, lane);
     }
 
     if (!ok) return;
-    ok = warp_wait(&bars[Smem::kODone + wg], 0, ctl, FDS_STATUS_TIMEOUT_SOFTMAX);
+    ok = warp_wait(pv_done, (n_tiles - 1) & 1, ctl, FDS_STATUS_TIMEOUT_SOFTMAX);
     if (!ok) return;
     tc_fence_after();
     uint32_t o[64];
@@ -324,6 +363,9 @@ __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint
     }
 }
 
+// The whole MMA warp walks the schedule (waits are warp-collective); one
+// elected lane issues each group of tcgen05.mma and its commits, so the
+// descriptors stay warp-uniform and the tensor pipe is fed at full rate.
 template <typename T, bool kRelBias>
 __device__ __forceinline__ void mma_role(uint8_t* smem, uint64_t* bars, uint32_t tmem, const AttnParams& p,
                                          const WaitCtl& ctl, int n_tiles, bool has_q1) {
@@ -334,7 +376,7 @@ __device__ __forceinline__ void mma_role(uint8_t* smem, uint64_t* bars, uint32_t
     constexpr int err = FDS_STATUS_TIMEOUT_MMA;
 
     bool ok = true;
-    if (p.debug_flags & FDS_DEBUG_FORCE_TIMEOUT) ok = wait_bounded(&bars[Smem::kNever], 0, ctl, err);
+    if (p.debug_flags & FDS_DEBUG_FORCE_TIMEOUT) ok = warp_wait(&bars[Smem::kNever], 0, ctl, err);
     bool issued_any = false;
 
     if (ok && n_tiles > 0) {
@@ -343,76 +385,101 @@ __device__ __forceinline__ void mma_role(uint8_t* smem, uint64_t* bars, uint32_t
         const uint64_t dq1 = sw128_desc(smem_u32(smem + Smem::q1));
         const uint32_t dk0 = smem_u32(smem + Smem::k);
         const uint32_t dv0 = smem_u32(smem + Smem::v);
-        uint32_t p_parity = 0;  // bit w: next P phase of query tile w
+        uint32_t free_par = 0;  // bit w: next s_free phase of query tile w
+        uint32_t p_par = 0;     // bit w: next p_full phase of query tile w
 
-        ok = wait_bounded(&bars[Smem::kQ], 0, ctl, err);
+        ok = warp_wait(&bars[Smem::kQ], 0, ctl, err);
         if (ok) {
             tc_fence_after();
-            issued_any = kRelBias;
             if constexpr (kRelBias) {
-                const uint64_t dr = sw128_desc(smem_u32(smem + Smem::rel));
-                for (int w = 0; w < nq; ++w) {
+                issued_any = true;
+                if (elect_one()) {
+                    const uint64_t dr = sw128_desc(smem_u32(smem + Smem::rel));
+                    for (int w = 0; w < nq; ++w) {
 #pragma unroll
-                    for (int k = 0; k < kHeadDim / 16; ++k)
-                        mma_ss(tmem + w * kBlockN, (w ? dq1 : dq0) + 2 * k, dr + 2 * k, kIdescQR, k > 0);
-                    mma_commit(&bars[Smem::kSFull + w]);
+                        for (int k = 0; k < kHeadDim / 16; ++k)
+                            mma_ss(tmem + kTmemS + w * kBlockN, (w ? dq1 : dq0) + 2 * k, dr + 2 * k, kIdescQR, k > 0);
+                        mma_commit(&bars[Smem::kSFull + w]);
+                    }
                 }
+                __syncwarp();
             }
-            ok = wait_bounded(&bars[Smem::kKFull + 0], 0, ctl, err);
+            ok = warp_wait(&bars[Smem::kKFull + 0], 0, ctl, err);
         }
         // S(0) for each query tile (after its QR copy has left the S columns)
         for (int w = 0; ok && w < nq; ++w) {
             if constexpr (kRelBias) {
-                ok = wait_bounded(&bars[Smem::kPFull + w], (p_parity >> w) & 1, ctl, err);
-                p_parity ^= 1u << w;
+                ok = warp_wait(&bars[Smem::kSFree + w], (free_par >> w) & 1, ctl, err);
+                free_par ^= 1u << w;
                 if (!ok) break;
             }
             tc_fence_after();
             issued_any = true;
-            const uint64_t dk = sw128_desc(dk0);
+            if (elect_one()) {
+                const uint64_t dk = sw128_desc(dk0);
 #pragma unroll
-            for (int k = 0; k < kHeadDim / 16; ++k)
-                mma_ss(tmem + w * kBlockN, (w ? dq1 : dq0) + 2 * k, dk + 2 * k, kIdescQK, k > 0);
-            mma_commit(&bars[Smem::kSFull + w]);
+                for (int k = 0; k < kHeadDim / 16; ++k)
+                    mma_ss(tmem + kTmemS + w * kBlockN, (w ? dq1 : dq0) + 2 * k, dk + 2 * k, kIdescQK, k > 0);
+                mma_commit(&bars[Smem::kSFull + w]);
+                if (w == nq - 1) mma_commit(&bars[Smem::kKEmpty + 0]);
+            }
+            __syncwarp();
         }
-        for (int j = 0; ok && j < n_tiles; ++j) {
-            const int st = j % kStages;
-            ok = wait_bounded(&bars[Smem::kVFull + st], (j / kStages) & 1, ctl, err);
-            if (!ok) break;
-            const uint64_t dv = sw128_desc(dv0 + st * kTileBytes);
-            const bool more = j + 1 < n_tiles;
-            const int st1 = (j + 1) % kStages;
-            for (int w = 0; w < nq; ++w) {
-                ok = wait_bounded(&bars[Smem::kPFull + w], (p_parity >> w) & 1, ctl, err);
-                p_parity ^= 1u << w;
-                if (!ok) break;
-                tc_fence_after();
+        // Steady-state service order, matching the order in which the two
+        // softmax warpgroups (Q1 half a tile behind Q0) raise their signals:
+        //   S0(j+1), P1(j-1) V, S1(j+1), P0(j) V
+        auto issue_s = [&](int w, int jn) {  // S_w(jn) = Q_w K(jn)^T once S_w(jn-1) has left TMEM
+            ok = warp_wait(&bars[Smem::kSFree + w], (free_par >> w) & 1, ctl, err);
+            free_par ^= 1u << w;
+            if (!ok) return;
+            tc_fence_after();
+            const int stn = jn % kStages;
+            if (elect_one()) {
+                const uint64_t dk = sw128_desc(dk0 + stn * kTileBytes);
+#pragma unroll
+                for (int k = 0; k < kHeadDim / 16; ++k)
+                    mma_ss(tmem + kTmemS + w * kBlockN, (w ? dq1 : dq0) + 2 * k, dk + 2 * k, kIdescQK, k > 0);
+                mma_commit(&bars[Smem::kSFull + w]);
+                if (w == nq - 1) mma_commit(&bars[Smem::kKEmpty + stn]);  // last reader of K(jn)
+            }
+            __syncwarp();
+        };
+        auto issue_pv = [&](int w, int jp) {  // O_w += P_w(jp) V(jp)
+            ok = warp_wait(&bars[Smem::kPFull + w], (p_par >> w) & 1, ctl, err);
+            p_par ^= 1u << w;
+            if (!ok) return;
+            tc_fence_after();
+            const int stp = jp % kStages;
+            if (elect_one()) {
+                const uint64_t dv = sw128_desc(dv0 + stp * kTileBytes);
 #pragma unroll
                 for (int k = 0; k < kBlockN / 16; ++k)
-                    mma_ts(tmem + kTmemO + w * kHeadDim, tmem + w * kBlockN + 8 * k, dv + 128 * k, kIdescPV,
-                           (j > 0 || k > 0) ? 1u : 0u);
-                if (w == nq - 1) mma_commit(&bars[Smem::kKvEmpty + st]);
-                if (more) {
-                    if (w == 0) {
-                        ok = wait_bounded(&bars[Smem::kKFull + st1], ((j + 1) / kStages) & 1, ctl, err);
-                        if (!ok) break;
-                        tc_fence_after();
-                    }
-                    const uint64_t dk = sw128_desc(dk0 + st1 * kTileBytes);
-#pragma unroll
-                    for (int k = 0; k < kHeadDim / 16; ++k)
-                        mma_ss(tmem + w * kBlockN, (w ? dq1 : dq0) + 2 * k, dk + 2 * k, kIdescQK, k > 0);
-                    mma_commit(&bars[Smem::kSFull + w]);
-                } else {
-                    mma_commit(&bars[Smem::kODone + w]);
-                }
+                    mma_ts(tmem + kTmemO + w * kHeadDim, tmem + kTmemP + w * (kBlockN / 2) + 8 * k, dv + 128 * k,
+                           kIdescPV, (jp > 0 || k > 0) ? 1u : 0u);
+                mma_commit(&bars[Smem::kPvDone + w]);
+                if (w == nq - 1) mma_commit(&bars[Smem::kVEmpty + stp]);  // last reader of V(jp)
             }
+            __syncwarp();
+        };
+        for (int j = 0; ok && j < n_tiles; ++j) {
+            const bool more = j + 1 < n_tiles;
+            if (more) {
+                ok = warp_wait(&bars[Smem::kKFull + (j + 1) % kStages], ((j + 1) / kStages) & 1, ctl, err);
+                if (ok) issue_s(0, j + 1);
+            }
+            if (ok && nq == 2 && j > 0) issue_pv(1, j - 1);
+            if (ok && nq == 2 && more) issue_s(1, j + 1);
+            if (ok) ok = warp_wait(&bars[Smem::kVFull + j % kStages], (j / kStages) & 1, ctl, err);
+            if (ok) issue_pv(0, j);
         }
+        if (ok && nq == 2) issue_pv(1, n_tiles - 1);
     }
     // drain: every MMA issued above completes before TMEM is released
     if (issued_any) {
-        mma_commit(&bars[Smem::kDrain]);
+        if (elect_one()) mma_commit(&bars[Smem::kDrain]);
+        __syncwarp();
         wait_bounded(&bars[Smem::kDrain], 0, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
+        __syncwarp();
     }
 }
 
@@ -422,26 +489,45 @@ __device__ __forceinline__ void load_role(uint8_t* smem, uint64_t* bars, const C
                                           const CUtensorMap* map_r, const AttnParams& p, const WaitCtl& ctl,
                                           int b, int h, int q_base, int n_tiles, bool has_q1) {
     if (n_tiles == 0) return;
-    const uint32_t q_bytes = (has_q1 ? 2 : 1) * kTileBytes + (kRelBias ? kRelRows * 128 : 0);
-    mbar_arrive_expect_tx(&bars[Smem::kQ], q_bytes);
-    tma_load_3d(smem + Smem::q0, map_q, &bars[Smem::kQ], p.q_x0 + h * kHeadDim, q_base, b);
-    if (has_q1) tma_load_3d(smem + Smem::q1, map_q, &bars[Smem::kQ], p.q_x0 + h * kHeadDim, q_base + kBlockM, b);
-    if constexpr (kRelBias) tma_load_2d(smem + Smem::rel, map_r, &bars[Smem::kQ], 0, 0);
+    if (elect_one()) {
+        const uint32_t q_bytes = (has_q1 ? 2 : 1) * kTileBytes + (kRelBias ? kRelRows * 128 : 0);
+        mbar_arrive_expect_tx(&bars[Smem::kQ], q_bytes);
+        tma_load_3d(smem + Smem::q0, map_q, &bars[Smem::kQ], p.q_x0 + h * kHeadDim, q_base, b);
+        if (has_q1)
+            tma_load_3d(smem + Smem::q1, map_q, &bars[Smem::kQ], p.q_x0 + h * kHeadDim, q_base + kBlockM, b);
+        if constexpr (kRelBias) tma_load_2d(smem + Smem::rel, map_r, &bars[Smem::kQ], 0, 0);
+    }
+    __syncwarp();
 
     int issued_tiles = 0;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
         const int st = j % kStages;
+        const uint32_t par = ((j / kStages) - 1) & 1;
         if (j >= kStages) {
-            ok = wait_bounded(&bars[Smem::kKvEmpty + st], ((j / kStages) - 1) & 1, ctl, FDS_STATUS_TIMEOUT_LOAD);
+            ok = warp_wait(&bars[Smem::kKEmpty + st], par, ctl, FDS_STATUS_TIMEOUT_LOAD);
             if (!ok) break;
         }
-        mbar_arrive_expect_tx(&bars[Smem::kKFull + st], kTileBytes);
-        tma_load_3d(smem + Smem::k + st * kTileBytes, map_k, &bars[Smem::kKFull + st], p.k_x0 + h * kHeadDim,
-                    j * kBlockN, b);
-        mbar_arrive_expect_tx(&bars[Smem::kVFull + st], kTileBytes);
-        tma_load_3d(smem + Smem::v + st * kTileBytes, map_v, &bars[Smem::kVFull + st], p.v_x0 + h * kHeadDim,
-                    j * kBlockN, b);
+        if (elect_one()) {
+            mbar_arrive_expect_tx(&bars[Smem::kKFull + st], kTileBytes);
+            tma_load_3d(smem + Smem::k + st * kTileBytes, map_k, &bars[Smem::kKFull + st], p.k_x0 + h * kHeadDim,
+                        j * kBlockN, b);
+        }
+        __syncwarp();
+        if (j >= kStages) {
+            ok = warp_wait(&bars[Smem::kVEmpty + st], par, ctl, FDS_STATUS_TIMEOUT_LOAD);
+            if (!ok) {
+                // K(j) was issued but V(j) was not: drain K(j) here
+                wait_bounded(&bars[Smem::kKFull + st], (j / kStages) & 1, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
+                break;
+            }
+        }
+        if (elect_one()) {
+            mbar_arrive_expect_tx(&bars[Smem::kVFull + st], kTileBytes);
+            tma_load_3d(smem + Smem::v + st * kTileBytes, map_v, &bars[Smem::kVFull + st], p.v_x0 + h * kHeadDim,
+                        j * kBlockN, b);
+        }
+        __syncwarp();
         ++issued_tiles;
     }
     if (!ok) {
@@ -454,6 +540,7 @@ __device__ __forceinline__ void load_role(uint8_t* smem, uint64_t* bars, const C
             wait_bounded(&bars[Smem::kKFull + s], (n - 1) & 1, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
             wait_bounded(&bars[Smem::kVFull + s], (n - 1) & 1, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
         }
+        __syncwarp();
     }
 }
 
@@ -484,12 +571,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&bars[Smem::kKFull + s], 1);
             mbar_init(&bars[Smem::kVFull + s], 1);
-            mbar_init(&bars[Smem::kKvEmpty + s], 1);
+            mbar_init(&bars[Smem::kKEmpty + s], 1);
+            mbar_init(&bars[Smem::kVEmpty + s], 1);
         }
         for (int w = 0; w < 2; ++w) {
             mbar_init(&bars[Smem::kSFull + w], 1);
-            mbar_init(&bars[Smem::kPFull + w], kBlockM);
-            mbar_init(&bars[Smem::kODone + w], 1);
+            mbar_init(&bars[Smem::kSFree + w], 4);   // one arrival per softmax warp
+            mbar_init(&bars[Smem::kPFull + w], 4);
+            mbar_init(&bars[Smem::kPvDone + w], 1);
         }
         mbar_init(&bars[Smem::kDrain], 1);
         mbar_init(&bars[Smem::kNever], 1);
@@ -513,20 +602,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_holder;
     const WaitCtl ctl{abort_flag, p.status, p.timeout_ns > 0 ? p.timeout_ns : kDefaultTimeoutNs};
 
+    // The two register classes never share code again: each branch ends with
+    // its own arrival on the CTA-wide barrier (every thread of the CTA arrives
+    // exactly once, so all roles have finished with TMEM when it opens).
     if (warp < kMmaWarp) {
+        setmaxnreg_inc<kSoftmaxRegs>();
         softmax_role<T, kRelBias>(smem, bars, tmem, p, ctl, warp, lane, b, h, q_base, kv_end, n_tiles, has_q1);
-    } else if (warp == kMmaWarp) {
-        if (lane == 0) mma_role<T, kRelBias>(smem, bars, tmem, p, ctl, n_tiles, has_q1);
+        __syncwarp();
+        tc_fence_before();
+        named_barrier_sync(1, kThreads);
     } else {
-        if (lane == 0)
+        setmaxnreg_dec<kControlRegs>();
+        if (warp == kMmaWarp)
+            mma_role<T, kRelBias>(smem, bars, tmem, p, ctl, n_tiles, has_q1);
+        else if (warp == kLoadWarp)
             load_role<kRelBias>(smem, bars, &map_q, &map_k, &map_v, &map_r, p, ctl, b, h, q_base, n_tiles, has_q1);
-    }
-    __syncwarp();
-    tc_fence_before();
-    __syncthreads();
-    if (warp == kMmaWarp) {
-        tc_fence_after();
-        tmem_dealloc(tmem, kTmemCols);
+        __syncwarp();
+        tc_fence_before();
+        named_barrier_sync(1, kThreads);
+        if (warp == kMmaWarp) {
+            tc_fence_after();
+            tmem_dealloc(tmem, kTmemCols);
+        }
     }
 }
 

@@ -21,6 +21,36 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 
+// True in exactly one (the lowest) active lane of a converged warp.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n\t.reg .pred P1;\n\t"
+        "elect.sync _|P1, %1;\n\t"
+        "@P1 mov.s32 %0, 1;\n\t}"
+        : "+r"(pred)
+        : "r"(0xffffffffu));
+    return pred != 0;
+}
+
+// Per-warpgroup register reallocation (all four warps of a warpgroup execute
+// the same instruction). The increase waits until the pool launched with the
+// CTA (threads x launch registers) can satisfy it, so every split must sum to
+// at most that pool; the build checks the launch register count it relies on.
+template <uint32_t kRegs>
+__device__ __forceinline__ void setmaxnreg_inc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <uint32_t kRegs>
+__device__ __forceinline__ void setmaxnreg_dec() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
+// Named CTA barrier `id` over `count` threads (a multiple of 32).
+__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -220,10 +250,60 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int ab_format, in
 
 // ---------------------------------------------------------------- math
 
+// Packed fp32 pair arithmetic (sm_100 f32x2): one instruction, two lanes of work.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+// max(a, b, c) in one instruction (sm_100 three-input max)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// 2^x for a pair on the FMA pipe (keeps the MUFU free for the other pairs).
+// x = j + f with j = round(x) from the 1.5 * 2^23 shifter (t = x + C holds j
+// in its low mantissa bits, t - C = j exactly), f = x - j in [-1/2, 1/2];
+// q(f) ~ 2^f is a cubic minimax fit of the relative error (max 7.5e-5, see
+// fit_exp2_poly.py), and 2^j enters by adding j to q's exponent field. x is
+// clamped to >= -125 so that the exponent field stays normal (2^-125 is
+// indistinguishable from 0 next to the row sum, which is >= 1).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+    x.x = fmaxf(x.x, -125.0f);
+    x.y = fmaxf(x.y, -125.0f);
+    const float2 t = fadd2(x, make_float2(kShift, kShift));
+    const float2 r = fadd2(t, make_float2(-kShift, -kShift));
+    const float2 f = fadd2(x, make_float2(-r.x, -r.y));
+    float2 q = ffma2(make_float2(0.0551716685295105f, 0.0551716685295105f), f,
+                     make_float2(0.2426111251115799f, 0.2426111251115799f));
+    q = ffma2(q, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+    q = ffma2(q, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
+    return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                       __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
 }
 
 }  // namespace fds

@@ -67,6 +67,18 @@ def flexrel_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rel: torch.T
     return out
 
 
+def flexrel_rows(q, k, v, rel, start: int, stop: int) -> torch.Tensor:
+    """Rows [start, stop) of :func:`flexrel_core` (no mask): one chunk of
+    torch_core_chunked (flexrel_triton.py:312-328). Used to time the CPU path."""
+    batch, heads, length, dim = q.shape
+    qc = q[:, :, start:stop].float()
+    idx = rel_index(length, start, stop)
+    qr = torch.einsum("bhld,rd->bhlr", qc, rel.float())
+    bias = torch.gather(qr, 3, idx.view(1, 1, stop - start, length).expand(batch, heads, -1, -1))
+    scores = (qc @ k.float().transpose(-2, -1) + bias) * (1.0 / math.sqrt(dim))
+    return torch.softmax(scores, dim=-1) @ v.float()
+
+
 def split_qkv(qkv: torch.Tensor, batch: int, heads: int):
     """[B*L, 3*H*D] (q | k | v column blocks) -> three [B, H, L, D] fp32 views."""
     rows, width = qkv.shape
