@@ -2,21 +2,24 @@
 //
 // One CTA owns 256 query rows of one (window, head): two 128-row query tiles
 // (Q0, Q1) that share every K/V tile. Warp roles (384 threads, 3 warpgroups):
-//   warps 0-3  softmax for Q0 (thread = query row = TMEM lane)
-//   warps 4-7  softmax for Q1
-//   warp  8    MMA issuer (whole warp runs the schedule, one elected lane
-//              issues each group of tcgen05.mma) and TMEM owner
-//   warp  9    TMA producer (same convention)
-//   warps 10-11 idle (complete the third warpgroup)
-// Registers: launched at 168 per thread; the third warpgroup gives back down
-// to 56 and the two softmax warpgroups take 224 (256*224 + 128*56 = 384*168),
-// enough to hold a row of S (128 fp32) and of P (64 packed pairs) at once.
+//   warpgroup 0 (warps 0-3)  softmax of query tile 0 (thread = query row = TMEM lane)
+//   warpgroup 1 (warps 4-7)  softmax of query tile 1
+//   warp 8                   MMA issuer of query tile 0
+//   warp 9                   TMA producer (K / V ring, Q, the rel table)
+//   warp 10                  MMA issuer of query tile 1
+//   warp 11                  TMEM owner (allocates / releases the 512 columns)
+// Each query tile has its own MMA warp, which serves that tile's hand-offs in
+// their natural order (S(j+1) once S(j) is read out, P(j) V(j) once P(j) is
+// stored); one MMA warp serving both tiles in a fixed order made each tile
+// wait on the other's progress.
+// tcgen05.mma groups are issued by one elected lane of a converged warp, so
+// the descriptors are warp-uniform and the tensor pipe is fed at full rate.
+//
 // TMEM (512 columns): S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384)
 //                     O0 [384,448) O1 [448,512).
 // P (the exponentiated scores, two 16-bit values per column) has its own
-// columns, so S(j+1) = Q K(j+1)^T is issued as soon as the softmax warps have
-// pulled S(j) into registers and runs under their exponentials, and
-// P(j) V(j) runs under the next tile's softmax.
+// columns, so S(j+1) = Q K(j+1)^T runs while the softmax warps exponentiate
+// S(j), and P(j) V(j) runs under the next tile's softmax.
 //
 // Relative bias (encoder): bias(i, j) = q_i . rel[clamp(j - i, -64, 8) + 64].
 // Per query tile the MMA computes QR = Q . rel^T (N = 80, rows 73..79 zero)
@@ -32,6 +35,10 @@
 // Online softmax: log2 units, lazy rescaling (the running max used for the
 // exponent only moves when a tile's max exceeds it by more than 8, i.e. P is
 // bounded by 256), fp32 row sums, P rounded to the operand type.
+//
+// Registers: launched at 168 per thread; the third warpgroup gives back down
+// to 40 and the two softmax warpgroups take 232 (256*232 + 128*40 = 384*168),
+// enough to hold a row of S (128 fp32) and of P (64 packed pairs) at once.
 //
 // Every wait is bounded by a globaltimer deadline; an expired wait records a
 // status bit, raises a CTA-wide abort flag, and every role then drains its
@@ -60,13 +67,15 @@ constexpr int kClampLeft = 64;
 constexpr int kClampRight = 8;
 constexpr int kRelRows = 80;       // table rows padded to a multiple of 16 (MMA N)
 constexpr int kQrStride = 74;      // floats per row of the shared QR copy (conflict-free gather)
-constexpr int kMmaWarp = 8;
+constexpr int kMmaWarp0 = 8;       // MMA issuer of query tile 0 (tile 1: kMmaWarp0 + 2)
 constexpr int kLoadWarp = 9;
+constexpr int kTmemWarp = 11;
 constexpr int kThreads = 384;
-constexpr int kLaunchRegs = 168;     // per thread at launch (checked at build time)
+constexpr int kLaunchRegs = 168;   // per thread at launch (checked at build time)
 constexpr int kSoftmaxRegs = 232;
 constexpr int kControlRegs = 40;
-static_assert(256 * kSoftmaxRegs + 128 * kControlRegs <= kThreads * kLaunchRegs, "register split exceeds the launch pool");
+static_assert(256 * kSoftmaxRegs + 128 * kControlRegs <= kThreads * kLaunchRegs,
+              "register split exceeds the launch pool");
 constexpr int kTmemCols = 512;
 constexpr int kTmemS = 0;          // S_w at kTmemS + 128 w
 constexpr int kTmemP = 256;        // P_w at kTmemP + 64 w
@@ -86,14 +95,14 @@ struct Smem {
     static constexpr int kQ = 0;
     static constexpr int kKFull = 1;
     static constexpr int kVFull = kKFull + kStages;
-    static constexpr int kKEmpty = kVFull + kStages;    // MMA -> producer: K stage consumed
-    static constexpr int kVEmpty = kKEmpty + kStages;   // MMA -> producer: V stage consumed
-    static constexpr int kSFull = kVEmpty + kStages;    // MMA -> softmax: S(j) (or QR) in TMEM
-    static constexpr int kSFree = kSFull + 2;           // softmax -> MMA: S(j) read into registers
-    static constexpr int kPFull = kSFree + 2;           // softmax -> MMA: P(j) in TMEM, O rescaled
-    static constexpr int kPvDone = kPFull + 2;          // MMA -> softmax: P(j) V(j) complete
-    static constexpr int kDrain = kPvDone + 2;
-    static constexpr int kNever = kDrain + 1;
+    static constexpr int kKEmpty = kVFull + kStages;    // S MMAs of every query tile done with a K stage
+    static constexpr int kVEmpty = kKEmpty + kStages;   // P V MMAs of every query tile done with a V stage
+    static constexpr int kSFull = kVEmpty + kStages;    // S(j) (or QR) in TMEM          [per query tile]
+    static constexpr int kSFree = kSFull + 2;           // all 4 warps read S(j) out     [per query tile]
+    static constexpr int kPFull = kSFree + 2;           // all 4 warps stored P(j)       [per query tile]
+    static constexpr int kPvDone = kPFull + 2;          // P(j) V(j) complete            [per query tile]
+    static constexpr int kDrain = kPvDone + 2;          // per query tile: its MMA warp's drain
+    static constexpr int kNever = kDrain + 2;
     static constexpr int kNumBars = kNever + 1;
     static constexpr int misc = bars + kNumBars * 8;
     static constexpr int total = misc + 16;
@@ -144,7 +153,7 @@ struct WaitCtl {
 // Returns false (after recording `err_bit` and raising the abort flag) on
 // expiry, or at once when another role has already aborted.
 __device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, const WaitCtl& ctl, int err_bit,
-                                          bool honour_abort = true) {
+                                             bool honour_abort = true) {
     const uint32_t addr = smem_u32(bar);
     if (mbar_try_wait(addr, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
@@ -178,12 +187,125 @@ __device__ __forceinline__ void warp_arrive(uint64_t* bar, int lane) {
     if (lane == 0) mbar_arrive(bar);
 }
 
+// Tensor-core work of one query tile (one elected lane of its MMA warp issues
+// every MMA and every commit that tracks them).
+template <typename T, bool kRelBias>
+struct TileMma {
+    static constexpr int fmt = DTypeTraits<T>::kFormat;
+    static constexpr uint32_t kIdescQK = idesc_f16(kBlockM, kBlockN, fmt, 0, 0);
+    static constexpr uint32_t kIdescQR = idesc_f16(kBlockM, kRelRows, fmt, 0, 0);
+    static constexpr uint32_t kIdescPV = idesc_f16(kBlockM, kHeadDim, fmt, 0, 1);
+
+    uint8_t* smem;
+    uint64_t* bars;
+    uint32_t tmem;
+    int w;  // query tile
+
+    __device__ __forceinline__ uint64_t q_desc() const {
+        return sw128_desc(smem_u32(smem + (w ? Smem::q1 : Smem::q0)));
+    }
+
+    __device__ __forceinline__ void qr() const {  // S_w columns <- Q_w rel^T
+        if (elect_one()) {
+            const uint64_t dq = q_desc();
+            const uint64_t dr = sw128_desc(smem_u32(smem + Smem::rel));
+#pragma unroll
+            for (int k = 0; k < kHeadDim / 16; ++k)
+                mma_ss(tmem + kTmemS + w * kBlockN, dq + 2 * k, dr + 2 * k, kIdescQR, k > 0);
+            mma_commit(&bars[Smem::kSFull + w]);
+        }
+        __syncwarp();
+    }
+
+    __device__ __forceinline__ void s(int jn) const {  // S_w columns <- Q_w K(jn)^T
+        if (elect_one()) {
+            const int st = jn % kStages;
+            const uint64_t dq = q_desc();
+            const uint64_t dk = sw128_desc(smem_u32(smem + Smem::k + st * kTileBytes));
+#pragma unroll
+            for (int k = 0; k < kHeadDim / 16; ++k)
+                mma_ss(tmem + kTmemS + w * kBlockN, dq + 2 * k, dk + 2 * k, kIdescQK, k > 0);
+            mma_commit(&bars[Smem::kSFull + w]);
+            mma_commit(&bars[Smem::kKEmpty + st]);
+        }
+        __syncwarp();
+    }
+
+    __device__ __forceinline__ void pv(int jp) const {  // O_w += P_w V(jp)
+        if (elect_one()) {
+            const int st = jp % kStages;
+            const uint64_t dv = sw128_desc(smem_u32(smem + Smem::v + st * kTileBytes));
+#pragma unroll
+            for (int k = 0; k < kBlockN / 16; ++k)
+                mma_ts(tmem + kTmemO + w * kHeadDim, tmem + kTmemP + w * (kBlockN / 2) + 8 * k, dv + 128 * k,
+                       kIdescPV, (jp > 0 || k > 0) ? 1u : 0u);
+            mma_commit(&bars[Smem::kPvDone + w]);
+            mma_commit(&bars[Smem::kVEmpty + st]);
+        }
+        __syncwarp();
+    }
+
+    // every MMA this lane issued completes before TMEM can be released
+    __device__ __forceinline__ void drain(const WaitCtl& ctl) const {
+        if (elect_one()) mma_commit(&bars[Smem::kDrain + w]);
+        __syncwarp();
+        wait_bounded(&bars[Smem::kDrain + w], 0, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
+        __syncwarp();
+    }
+};
+
+// The MMA warp of query tile w: QR (encoder), then per KV tile S(j+1) once the
+// softmax warps have read S(j) out of TMEM and O += P(j) V(j) once they have
+// stored P(j).
+template <typename T, bool kRelBias>
+__device__ __forceinline__ void mma_role(uint8_t* smem, uint64_t* bars, uint32_t tmem, const WaitCtl& ctl, int w,
+                                         int n_tiles, bool has_q1) {
+    if (n_tiles == 0 || (w == 1 && !has_q1)) return;
+    const TileMma<T, kRelBias> mma{smem, bars, tmem, w};
+    constexpr int err = FDS_STATUS_TIMEOUT_MMA;
+    uint64_t* s_free = &bars[Smem::kSFree + w];
+    uint64_t* p_full = &bars[Smem::kPFull + w];
+    uint32_t free_parity = 0;
+    bool issued = false;
+    bool ok = warp_wait(&bars[Smem::kQ], 0, ctl, err);
+    if (ok && kRelBias) {
+        tc_fence_after();
+        mma.qr();
+        issued = true;
+        ok = warp_wait(s_free, free_parity, ctl, err);  // QR copied out of the S columns
+        free_parity ^= 1;
+    }
+    if (ok) ok = warp_wait(&bars[Smem::kKFull + 0], 0, ctl, err);
+    if (ok) {
+        tc_fence_after();
+        mma.s(0);
+        issued = true;
+    }
+    for (int j = 0; ok && j < n_tiles; ++j) {
+        if (j + 1 < n_tiles) {
+            ok = warp_wait(s_free, free_parity, ctl, err);
+            free_parity ^= 1;
+            if (ok) ok = warp_wait(&bars[Smem::kKFull + (j + 1) % kStages], ((j + 1) / kStages) & 1, ctl, err);
+            if (!ok) break;
+            tc_fence_after();
+            mma.s(j + 1);
+        }
+        ok = warp_wait(p_full, j & 1, ctl, err);
+        if (ok) ok = warp_wait(&bars[Smem::kVFull + j % kStages], (j / kStages) & 1, ctl, err);
+        if (!ok) break;
+        tc_fence_after();
+        mma.pv(j);
+    }
+    if (issued) mma.drain(ctl);
+}
+
 template <typename T, bool kRelBias>
 __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint32_t tmem, const AttnParams& p,
                                              const WaitCtl& ctl, int warp, int lane, int b, int h, int q_base,
                                              int kv_end, int n_tiles, bool has_q1) {
     const int wg = warp >> 2;                    // query tile of this warpgroup
-    const int row = ((warp & 3) << 5) + lane;    // row in tile == TMEM lane
+    const int wq = warp & 3;                     // warp within the warpgroup
+    const int row = (wq << 5) + lane;            // row in tile == TMEM lane
     const int i = q_base + wg * kBlockM + row;   // query index in the window
     const int L = p.seq_len;
     if (wg == 1 && !has_q1) return;
@@ -198,7 +320,8 @@ __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint
         return;
     }
 
-    const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    constexpr int err = FDS_STATUS_TIMEOUT_SOFTMAX;
+    const uint32_t lane_addr = static_cast<uint32_t>(wq * 32) << 16;
     const uint32_t tS = tmem + lane_addr + kTmemS + wg * kBlockN;
     const uint32_t tP = tmem + lane_addr + kTmemP + wg * (kBlockN / 2);
     const uint32_t tO = tmem + lane_addr + kTmemO + wg * kHeadDim;
@@ -209,11 +332,12 @@ __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint
     uint64_t* p_full = &bars[Smem::kPFull + wg];
     uint64_t* pv_done = &bars[Smem::kPvDone + wg];
 
-    float qr_left = 0.f, qr_right = 0.f;
-    uint32_t s_parity = 0;
     bool ok = true;
+    uint32_t s_parity = 0;      // next s_full phase
+    float qr_left = 0.f, qr_right = 0.f;
+
     if constexpr (kRelBias) {
-        ok = warp_wait(s_full, s_parity, ctl, FDS_STATUS_TIMEOUT_SOFTMAX);
+        ok = warp_wait(s_full, s_parity, ctl, err);
         s_parity ^= 1;
         if (ok) {
             tc_fence_after();
@@ -238,7 +362,7 @@ __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint
     float m_run = -INFINITY;
     float l_run = 0.f;
     for (int j = 0; ok && j < n_tiles; ++j) {
-        ok = warp_wait(s_full, s_parity, ctl, FDS_STATUS_TIMEOUT_SOFTMAX);
+        ok = warp_wait(s_full, s_parity, ctl, err);
         s_parity ^= 1;
         if (!ok) break;
         tc_fence_after();
@@ -249,7 +373,7 @@ __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint
         tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
         tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
         tmem_wait_ld();
-        warp_arrive(s_free, lane);  // the MMA may now compute S(j+1) into these columns
+        warp_arrive(s_free, lane);  // the MMA warp may now compute S(j+1) into these columns
         float s[128];
 #pragma unroll
         for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sr[c]);
@@ -320,7 +444,7 @@ __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint
         if (j > 0) {
             // P(j-1) V(j-1) must be complete before its P columns are rewritten
             // and before O is rescaled (its latency hides under the work above).
-            ok = warp_wait(pv_done, (j - 1) & 1, ctl, FDS_STATUS_TIMEOUT_SOFTMAX);
+            ok = warp_wait(pv_done, (j - 1) & 1, ctl, err);
             if (!ok) break;
             tc_fence_after();
         }
@@ -341,145 +465,25 @@ __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint
         warp_arrive(p_full, lane);
     }
 
-    if (!ok) return;
-    ok = warp_wait(pv_done, (n_tiles - 1) & 1, ctl, FDS_STATUS_TIMEOUT_SOFTMAX);
-    if (!ok) return;
-    tc_fence_after();
-    uint32_t o[64];
-    tmem_ld32(tO, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
-    tmem_ld32(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
-    tmem_wait_ld();
-    if (i < L) {
-        const float inv = 1.f / l_run;
+    if (ok) ok = warp_wait(pv_done, (n_tiles - 1) & 1, ctl, err);
+    if (ok) {
+        tc_fence_after();
+        uint32_t o[64];
+        tmem_ld32(tO, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+        tmem_ld32(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+        tmem_wait_ld();
+        if (i < L) {
+            const float inv = 1.f / l_run;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            uint4 v;
-            v.x = DTypeTraits<T>::pack(__uint_as_float(o[8 * c + 0]) * inv, __uint_as_float(o[8 * c + 1]) * inv);
-            v.y = DTypeTraits<T>::pack(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv);
-            v.z = DTypeTraits<T>::pack(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv);
-            v.w = DTypeTraits<T>::pack(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv);
-            reinterpret_cast<uint4*>(out_row)[c] = v;
+            for (int c = 0; c < 8; ++c) {
+                uint4 v;
+                v.x = DTypeTraits<T>::pack(__uint_as_float(o[8 * c + 0]) * inv, __uint_as_float(o[8 * c + 1]) * inv);
+                v.y = DTypeTraits<T>::pack(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv);
+                v.z = DTypeTraits<T>::pack(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv);
+                v.w = DTypeTraits<T>::pack(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv);
+                reinterpret_cast<uint4*>(out_row)[c] = v;
+            }
         }
-    }
-}
-
-// The whole MMA warp walks the schedule (waits are warp-collective); one
-// elected lane issues each group of tcgen05.mma and its commits, so the
-// descriptors stay warp-uniform and the tensor pipe is fed at full rate.
-template <typename T, bool kRelBias>
-__device__ __forceinline__ void mma_role(uint8_t* smem, uint64_t* bars, uint32_t tmem, const AttnParams& p,
-                                         const WaitCtl& ctl, int n_tiles, bool has_q1) {
-    constexpr int fmt = DTypeTraits<T>::kFormat;
-    constexpr uint32_t kIdescQK = idesc_f16(kBlockM, kBlockN, fmt, 0, 0);
-    constexpr uint32_t kIdescQR = idesc_f16(kBlockM, kRelRows, fmt, 0, 0);
-    constexpr uint32_t kIdescPV = idesc_f16(kBlockM, kHeadDim, fmt, 0, 1);
-    constexpr int err = FDS_STATUS_TIMEOUT_MMA;
-
-    bool ok = true;
-    if (p.debug_flags & FDS_DEBUG_FORCE_TIMEOUT) ok = warp_wait(&bars[Smem::kNever], 0, ctl, err);
-    bool issued_any = false;
-
-    if (ok && n_tiles > 0) {
-        const int nq = has_q1 ? 2 : 1;
-        const uint64_t dq0 = sw128_desc(smem_u32(smem + Smem::q0));
-        const uint64_t dq1 = sw128_desc(smem_u32(smem + Smem::q1));
-        const uint32_t dk0 = smem_u32(smem + Smem::k);
-        const uint32_t dv0 = smem_u32(smem + Smem::v);
-        uint32_t free_par = 0;  // bit w: next s_free phase of query tile w
-        uint32_t p_par = 0;     // bit w: next p_full phase of query tile w
-
-        ok = warp_wait(&bars[Smem::kQ], 0, ctl, err);
-        if (ok) {
-            tc_fence_after();
-            if constexpr (kRelBias) {
-                issued_any = true;
-                if (elect_one()) {
-                    const uint64_t dr = sw128_desc(smem_u32(smem + Smem::rel));
-                    for (int w = 0; w < nq; ++w) {
-#pragma unroll
-                        for (int k = 0; k < kHeadDim / 16; ++k)
-                            mma_ss(tmem + kTmemS + w * kBlockN, (w ? dq1 : dq0) + 2 * k, dr + 2 * k, kIdescQR, k > 0);
-                        mma_commit(&bars[Smem::kSFull + w]);
-                    }
-                }
-                __syncwarp();
-            }
-            ok = warp_wait(&bars[Smem::kKFull + 0], 0, ctl, err);
-        }
-        // S(0) for each query tile (after its QR copy has left the S columns)
-        for (int w = 0; ok && w < nq; ++w) {
-            if constexpr (kRelBias) {
-                ok = warp_wait(&bars[Smem::kSFree + w], (free_par >> w) & 1, ctl, err);
-                free_par ^= 1u << w;
-                if (!ok) break;
-            }
-            tc_fence_after();
-            issued_any = true;
-            if (elect_one()) {
-                const uint64_t dk = sw128_desc(dk0);
-#pragma unroll
-                for (int k = 0; k < kHeadDim / 16; ++k)
-                    mma_ss(tmem + kTmemS + w * kBlockN, (w ? dq1 : dq0) + 2 * k, dk + 2 * k, kIdescQK, k > 0);
-                mma_commit(&bars[Smem::kSFull + w]);
-                if (w == nq - 1) mma_commit(&bars[Smem::kKEmpty + 0]);
-            }
-            __syncwarp();
-        }
-        // Steady-state service order, matching the order in which the two
-        // softmax warpgroups (Q1 half a tile behind Q0) raise their signals:
-        //   S0(j+1), P1(j-1) V, S1(j+1), P0(j) V
-        auto issue_s = [&](int w, int jn) {  // S_w(jn) = Q_w K(jn)^T once S_w(jn-1) has left TMEM
-            ok = warp_wait(&bars[Smem::kSFree + w], (free_par >> w) & 1, ctl, err);
-            free_par ^= 1u << w;
-            if (!ok) return;
-            tc_fence_after();
-            const int stn = jn % kStages;
-            if (elect_one()) {
-                const uint64_t dk = sw128_desc(dk0 + stn * kTileBytes);
-#pragma unroll
-                for (int k = 0; k < kHeadDim / 16; ++k)
-                    mma_ss(tmem + kTmemS + w * kBlockN, (w ? dq1 : dq0) + 2 * k, dk + 2 * k, kIdescQK, k > 0);
-                mma_commit(&bars[Smem::kSFull + w]);
-                if (w == nq - 1) mma_commit(&bars[Smem::kKEmpty + stn]);  // last reader of K(jn)
-            }
-            __syncwarp();
-        };
-        auto issue_pv = [&](int w, int jp) {  // O_w += P_w(jp) V(jp)
-            ok = warp_wait(&bars[Smem::kPFull + w], (p_par >> w) & 1, ctl, err);
-            p_par ^= 1u << w;
-            if (!ok) return;
-            tc_fence_after();
-            const int stp = jp % kStages;
-            if (elect_one()) {
-                const uint64_t dv = sw128_desc(dv0 + stp * kTileBytes);
-#pragma unroll
-                for (int k = 0; k < kBlockN / 16; ++k)
-                    mma_ts(tmem + kTmemO + w * kHeadDim, tmem + kTmemP + w * (kBlockN / 2) + 8 * k, dv + 128 * k,
-                           kIdescPV, (jp > 0 || k > 0) ? 1u : 0u);
-                mma_commit(&bars[Smem::kPvDone + w]);
-                if (w == nq - 1) mma_commit(&bars[Smem::kVEmpty + stp]);  // last reader of V(jp)
-            }
-            __syncwarp();
-        };
-        for (int j = 0; ok && j < n_tiles; ++j) {
-            const bool more = j + 1 < n_tiles;
-            if (more) {
-                ok = warp_wait(&bars[Smem::kKFull + (j + 1) % kStages], ((j + 1) / kStages) & 1, ctl, err);
-                if (ok) issue_s(0, j + 1);
-            }
-            if (ok && nq == 2 && j > 0) issue_pv(1, j - 1);
-            if (ok && nq == 2 && more) issue_s(1, j + 1);
-            if (ok) ok = warp_wait(&bars[Smem::kVFull + j % kStages], (j / kStages) & 1, ctl, err);
-            if (ok) issue_pv(0, j);
-        }
-        if (ok && nq == 2) issue_pv(1, n_tiles - 1);
-    }
-    // drain: every MMA issued above completes before TMEM is released
-    if (issued_any) {
-        if (elect_one()) mma_commit(&bars[Smem::kDrain]);
-        __syncwarp();
-        wait_bounded(&bars[Smem::kDrain], 0, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
-        __syncwarp();
     }
 }
 
@@ -567,12 +571,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n_tiles = (kv_end + kBlockN - 1) / kBlockN;
 
     if (threadIdx.x == 0) {
+        const uint32_t nq = has_q1 ? 2 : 1;  // query tiles releasing each K / V stage
         mbar_init(&bars[Smem::kQ], 1);
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&bars[Smem::kKFull + s], 1);
             mbar_init(&bars[Smem::kVFull + s], 1);
-            mbar_init(&bars[Smem::kKEmpty + s], 1);
-            mbar_init(&bars[Smem::kVEmpty + s], 1);
+            mbar_init(&bars[Smem::kKEmpty + s], nq);
+            mbar_init(&bars[Smem::kVEmpty + s], nq);
         }
         for (int w = 0; w < 2; ++w) {
             mbar_init(&bars[Smem::kSFull + w], 1);
@@ -580,7 +585,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bars[Smem::kPFull + w], 4);
             mbar_init(&bars[Smem::kPvDone + w], 1);
         }
-        mbar_init(&bars[Smem::kDrain], 1);
+        for (int d = 0; d < 2; ++d) mbar_init(&bars[Smem::kDrain + d], 1);
         mbar_init(&bars[Smem::kNever], 1);
         *abort_flag = 0;
         fence_barrier_init();
@@ -592,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tensormap(&map_v);
         if (kRelBias) prefetch_tensormap(&map_r);
     }
-    if (warp == kMmaWarp) {
+    if (warp == kTmemWarp) {
         tmem_alloc(tmem_holder, kTmemCols);
         tmem_relinquish();
     }
@@ -605,7 +610,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // The two register classes never share code again: each branch ends with
     // its own arrival on the CTA-wide barrier (every thread of the CTA arrives
     // exactly once, so all roles have finished with TMEM when it opens).
-    if (warp < kMmaWarp) {
+    if (warp < kMmaWarp0) {
         setmaxnreg_inc<kSoftmaxRegs>();
         softmax_role<T, kRelBias>(smem, bars, tmem, p, ctl, warp, lane, b, h, q_base, kv_end, n_tiles, has_q1);
         __syncwarp();
@@ -613,14 +618,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_barrier_sync(1, kThreads);
     } else {
         setmaxnreg_dec<kControlRegs>();
-        if (warp == kMmaWarp)
-            mma_role<T, kRelBias>(smem, bars, tmem, p, ctl, n_tiles, has_q1);
-        else if (warp == kLoadWarp)
+        if (warp == kMmaWarp0 || warp == kMmaWarp0 + 2) {
+            // test hook: a wait on a barrier that nothing arrives on, to exercise
+            // the bounded-wait error path without a real hang
+            bool go = true;
+            if (p.debug_flags & FDS_DEBUG_FORCE_TIMEOUT)
+                go = warp_wait(&bars[Smem::kNever], 0, ctl, FDS_STATUS_TIMEOUT_MMA);
+            if (go) mma_role<T, kRelBias>(smem, bars, tmem, ctl, (warp - kMmaWarp0) >> 1, n_tiles, has_q1);
+        } else if (warp == kLoadWarp) {
             load_role<kRelBias>(smem, bars, &map_q, &map_k, &map_v, &map_r, p, ctl, b, h, q_base, n_tiles, has_q1);
+        }
         __syncwarp();
         tc_fence_before();
         named_barrier_sync(1, kThreads);
-        if (warp == kMmaWarp) {
+        if (warp == kTmemWarp) {
             tc_fence_after();
             tmem_dealloc(tmem, kTmemCols);
         }
