@@ -2,12 +2,16 @@
 //
 // One CTA owns 256 query rows of one (window, head): two 128-row query tiles
 // (Q0, Q1) that share every K/V tile. Warp roles (384 threads, 3 warpgroups):
-//   warpgroup 0 (warps 0-3)  softmax of query tile 0 (thread = query row = TMEM lane)
-//   warpgroup 1 (warps 4-7)  softmax of query tile 1
-//   warp 8                   MMA issuer of query tile 0
-//   warp 9                   TMA producer (K / V ring, Q, the rel table)
-//   warp 10                  MMA issuer of query tile 1
-//   warp 11                  TMEM owner (allocates / releases the 512 columns)
+//   warp 0                   MMA issuer of query tile 0
+//   warp 1                   TMA producer (K / V ring, Q, the rel table)
+//   warp 2                   MMA issuer of query tile 1
+//   warp 3                   TMEM owner (allocates / releases the 512 columns)
+//   warpgroup 1 (warps 4-7)  softmax of query tile 0 (thread = query row = TMEM lane)
+//   warpgroup 2 (warps 8-11) softmax of query tile 1
+// The control warps are the lowest-numbered (oldest) warps, which the warp
+// schedulers favour when several warps are ready: their few instructions
+// are on every hand-off's path, while the softmax warps always have
+// independent work to issue.
 // Each query tile has its own MMA warp, which serves that tile's hand-offs in
 // their natural order (S(j+1) once S(j) is read out, P(j) V(j) once P(j) is
 // stored); one MMA warp serving both tiles in a fixed order made each tile
@@ -36,7 +40,7 @@
 // exponent only moves when a tile's max exceeds it by more than 8, i.e. P is
 // bounded by 256), fp32 row sums, P rounded to the operand type.
 //
-// Registers: launched at 168 per thread; the third warpgroup gives back down
+// Registers: launched at 168 per thread; the control warpgroup gives back down
 // to 40 and the two softmax warpgroups take 232 (256*232 + 128*40 = 384*168),
 // enough to hold a row of S (128 fp32) and of P (64 packed pairs) at once.
 //
@@ -67,9 +71,10 @@ constexpr int kClampLeft = 64;
 constexpr int kClampRight = 8;
 constexpr int kRelRows = 80;       // table rows padded to a multiple of 16 (MMA N)
 constexpr int kQrStride = 74;      // floats per row of the shared QR copy (conflict-free gather)
-constexpr int kMmaWarp0 = 8;       // MMA issuer of query tile 0 (tile 1: kMmaWarp0 + 2)
-constexpr int kLoadWarp = 9;
-constexpr int kTmemWarp = 11;
+constexpr int kMmaWarp0 = 0;       // MMA issuer of query tile 0 (tile 1: kMmaWarp0 + 2)
+constexpr int kLoadWarp = 1;
+constexpr int kTmemWarp = 3;
+constexpr int kSoftmaxWarp0 = 4;   // first softmax warp (query tile 0: warps 4-7, tile 1: 8-11)
 constexpr int kThreads = 384;
 constexpr int kLaunchRegs = 168;   // per thread at launch (checked at build time)
 constexpr int kSoftmaxRegs = 232;
@@ -303,8 +308,8 @@ template <typename T, bool kRelBias>
 __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint32_t tmem, const AttnParams& p,
                                              const WaitCtl& ctl, int warp, int lane, int b, int h, int q_base,
                                              int kv_end, int n_tiles, bool has_q1) {
-    const int wg = warp >> 2;                    // query tile of this warpgroup
-    const int wq = warp & 3;                     // warp within the warpgroup
+    const int wg = (warp - kSoftmaxWarp0) >> 2;  // query tile of this warpgroup
+    const int wq = warp & 3;                     // warp within the warpgroup (= TMEM lane quarter)
     const int row = (wq << 5) + lane;            // row in tile == TMEM lane
     const int i = q_base + wg * kBlockM + row;   // query index in the window
     const int L = p.seq_len;
@@ -610,7 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // The two register classes never share code again: each branch ends with
     // its own arrival on the CTA-wide barrier (every thread of the CTA arrives
     // exactly once, so all roles have finished with TMEM when it opens).
-    if (warp < kMmaWarp0) {
+    if (warp >= kSoftmaxWarp0) {
         setmaxnreg_inc<kSoftmaxRegs>();
         softmax_role<T, kRelBias>(smem, bars, tmem, p, ctl, warp, lane, b, h, q_base, kv_end, n_tiles, has_q1);
         __syncwarp();

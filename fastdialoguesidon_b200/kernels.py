@@ -74,12 +74,16 @@ def _stream_ptr(device: torch.device) -> int:
 
 def _rows_operand(t: torch.Tensor, name: str) -> None:
     _check(isinstance(t, torch.Tensor), f"{name} must be a torch.Tensor")
-    _check(t.is_cuda, f"{name} must be a CUDA tensor (no CPU fallback)")
     _check(t.dim() == 2, f"{name} must be 2-D [rows, columns], got {tuple(t.shape)}")
     _check(t.dtype in _DTYPES, f"{name} must be float16 or bfloat16, got {t.dtype}")
     _check(t.stride(1) == 1, f"{name} columns must be contiguous (stride(1) == 1)")
     _check(t.shape[0] <= 1 or t.stride(0) % 8 == 0, f"{name} row stride must be a multiple of 8 elements")
     _check(t.data_ptr() % 16 == 0, f"{name} must be 16-byte aligned")
+
+
+def _on_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        _check(t.is_cuda, "tensors must be on a CUDA device (there is no CPU fallback)")
 
 
 def _raise_rc(rc: int, what: str) -> None:
@@ -124,10 +128,11 @@ def flexrel_attention(qkv: torch.Tensor, batch: int, heads: int, rel: torch.Tens
         _check(out.dtype == qkv.dtype and out.device == qkv.device, "out must match qkv's dtype and device")
     kv_ptr = None
     if kv_len is not None:
-        _check(isinstance(kv_len, torch.Tensor) and kv_len.is_cuda and kv_len.dtype == torch.int32
+        _check(isinstance(kv_len, torch.Tensor) and kv_len.dtype == torch.int32
                and kv_len.shape == (batch,) and kv_len.is_contiguous() and kv_len.device == qkv.device,
                f"kv_len must be a contiguous int32 CUDA tensor of shape [{batch}] on qkv's device")
         kv_ptr = kv_len.data_ptr()
+    _on_cuda(qkv, rel, out)
     dev = qkv.device
     lib = N.load()
     with torch.cuda.device(dev):
@@ -184,6 +189,7 @@ def rope_split(qkv: torch.Tensor, length: int, heads: int, cos: torch.Tensor,
     _check(hid % heads == 0 and hid // heads == HEAD_DIM, "head_dim must be 64")
     _check(length >= 1, "length must be >= 1")
     _rope_tables(cos, sin, min(length, rows) if rows else 1, qkv)
+    _on_cuda(qkv, cos, sin)
     out = torch.empty(3, rows, hid, device=qkv.device, dtype=qkv.dtype)
     lib = N.load()
     with torch.cuda.device(qkv.device):
@@ -225,6 +231,7 @@ def rope_attention(qkv: torch.Tensor, batch: int, heads: int, cos: torch.Tensor,
         _check(scratch.shape == (rows, 2 * hid) and scratch.is_contiguous() and scratch.dtype == qkv.dtype
                and scratch.device == qkv.device and scratch.data_ptr() % 16 == 0,
                f"scratch must be a contiguous [{rows}, {2 * hid}] {qkv.dtype} tensor on {qkv.device}")
+    _on_cuda(qkv, cos, sin, out, scratch)
     dev = qkv.device
     lib = N.load()
     with torch.cuda.device(dev):
