@@ -28,12 +28,15 @@ FDS_STATUS_TIMEOUT_DRAIN = 0x8
 
 FDS_DEBUG_FORCE_TIMEOUT = 0x1
 
+FDS_ROPE_STATIC_SCRATCH_BYTES = 20 * 1024 * 1024
+
 ABI_VERSION = 1
 
 # every symbol include/fds_b200.h declares (checked by the CPU test suite)
 EXPORTED_SYMBOLS = (
     "fds_flexrel_attn_fwd",
     "fds_rope_attn_fwd",
+    "fds_rope_attn_fwd_static",
     "fds_rope_split",
     "fds_abi_version",
     "fds_last_error",
@@ -108,6 +111,8 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         lib.fds_flexrel_attn_fwd.restype = ctypes.c_int
         lib.fds_rope_attn_fwd.argtypes = [ctypes.POINTER(FdsRopeArgs), ctypes.c_void_p]
         lib.fds_rope_attn_fwd.restype = ctypes.c_int
+        lib.fds_rope_attn_fwd_static.argtypes = [ctypes.POINTER(FdsRopeArgs), ctypes.c_void_p]
+        lib.fds_rope_attn_fwd_static.restype = ctypes.c_int
         lib.fds_rope_split.argtypes = [
             ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
             ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,

@@ -21,7 +21,7 @@ LIB_DIR = PKG_DIR / "_lib"
 LIB_PATH = LIB_DIR / "libfds_b200.so"
 INCLUDE_DIR = REPO_DIR / "include"
 
-SOURCES = ["fds_capi.cu"]
+SOURCES = ["fds_capi.cu", "fds_rope_static.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 # The attention kernels split their register file with setmaxnreg

@@ -11,6 +11,7 @@
 #include <string>
 
 #include "attn_kernel.cuh"
+#include "capi_internal.h"
 #include "fds_b200.h"
 #include "rope.cuh"
 
@@ -152,6 +153,16 @@ int check_common(const void* qkv, int64_t qkv_row_stride, const void* out, int64
 }
 
 }  // namespace
+
+int fds_detail::set_error(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
 
 extern "C" {
 

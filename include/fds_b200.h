@@ -118,6 +118,21 @@ FDS_API int fds_rope_split(const void* qkv, int64_t qkv_row_stride, const float*
                    void* out, int32_t rows, int32_t seq_len, int32_t heads, int32_t head_dim,
                    int32_t dtype, void* stream);
 
+/*
+ * Allocation-free variant of fds_rope_attn_fwd (no counterpart in the
+ * reference): for callers that cannot allocate device memory while running
+ * (an engine plugin's enqueue, a real-time callback, a serving loop with a
+ * fixed memory plan). The rotated q | k live in a static device array of
+ * FDS_ROPE_STATIC_SCRATCH_BYTES that every GPU loading it holds until exit
+ * (lazy module loading: from the first call on that GPU); args->qk_scratch
+ * must be NULL and batch*seq_len*2*heads*64
+ * 16-bit values must fit in it (else FDS_ERR_INVALID_ARGUMENT). The first call
+ * on a device resolves the array's address (make it before any stream
+ * capture). All calls share the array: calls that overlap on the GPU race.
+ */
+#define FDS_ROPE_STATIC_SCRATCH_BYTES (20u * 1024u * 1024u)
+FDS_API int fds_rope_attn_fwd_static(const FdsRopeArgs* args, void* stream);
+
 /* Version of this ABI (FDS_ABI_VERSION). */
 FDS_API int fds_abi_version(void);
 

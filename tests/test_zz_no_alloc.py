@@ -1,0 +1,69 @@
+"""fds_rope_attn_fwd_static: the DiT RoPE attention for callers that cannot
+allocate device memory while running (an engine plugin's enqueue, a real-time
+callback, a serving loop with a fixed memory plan). Its scratch is a static
+device array inside the library, so the caller passes only inputs and outputs.
+
+Checked through the C ABI against the regular entry point (which takes a
+caller-allocated scratch) on two calls in a row with different inputs, so
+stale contents of the shared static array would show. Tolerance as the rest of
+the suite: max-abs <= 2e-3 and SNR >= 55 dB.
+"""
+
+import ctypes
+import math
+
+import pytest
+import torch
+
+from fastdialoguesidon_b200 import _native as N
+from fastdialoguesidon_b200 import rope_tables
+from oracle import flexrel_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-3
+MIN_SNR = 55.0
+
+
+def _args(qkv, cos, sin, out, scratch, B, L, H, status):
+    return N.FdsRopeArgs(
+        qkv=qkv.data_ptr(), qkv_row_stride=qkv.stride(0), cos=cos.data_ptr(), sin=sin.data_ptr(),
+        qk_scratch=None if scratch is None else scratch.data_ptr(), out=out.data_ptr(),
+        out_row_stride=out.stride(0), status=status.data_ptr(), batch=B, heads=H, seq_len=L, head_dim=64,
+        dtype=N.FDS_DTYPE_FP16, scale=1.0 / math.sqrt(64), timeout_ns=0, debug_flags=0)
+
+
+def test_static_scratch_matches_allocating_entry_point(cuda_device):
+    lib = N.load()
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    status = torch.zeros(4, dtype=torch.int32, device=cuda_device)
+    for call, (B, L, H, seed) in enumerate([(2, 1000, 12, 1), (1, 6000, 12, 2)]):
+        gen = torch.Generator().manual_seed(seed)
+        qkv = (torch.randn(B * L, 3 * H * 64, generator=gen) * 0.55).half().to(cuda_device)
+        cos, sin = rope_tables(L, cuda_device)
+        out_ref = torch.empty(B * L, H * 64, dtype=torch.float16, device=cuda_device)
+        scratch = torch.empty(B * L, 2 * H * 64, dtype=torch.float16, device=cuda_device)
+        rc = lib.fds_rope_attn_fwd(ctypes.byref(_args(qkv, cos, sin, out_ref, scratch, B, L, H, status)), stream)
+        assert rc == N.FDS_OK, N.last_error()
+        out = torch.full_like(out_ref, float("nan"))
+        rc = lib.fds_rope_attn_fwd_static(ctypes.byref(_args(qkv, cos, sin, out, None, B, L, H, status)), stream)
+        assert rc == N.FDS_OK, N.last_error()
+        torch.cuda.synchronize(cuda_device)
+        assert int(status[0]) == 0
+        ref, got = out_ref.float().cpu(), out.float().cpu()
+        assert O.max_abs(ref, got) <= MAX_ABS and O.snr_db(ref, got) >= MIN_SNR, call
+
+
+def test_static_scratch_rejects_oversized_calls(cuda_device):
+    lib = N.load()
+    status = torch.zeros(4, dtype=torch.int32, device=cuda_device)
+    B, L, H = 2, 6000, 12   # 2 windows: 36.9 MB of rotated q|k > 20 MiB
+    qkv = torch.zeros(B * L, 3 * H * 64, dtype=torch.float16, device=cuda_device)
+    cos, sin = rope_tables(L, cuda_device)
+    out = torch.zeros(B * L, H * 64, dtype=torch.float16, device=cuda_device)
+    rc = lib.fds_rope_attn_fwd_static(ctypes.byref(_args(qkv, cos, sin, out, None, B, L, H, status)), None)
+    assert rc == N.FDS_ERR_INVALID_ARGUMENT
+    assert b"static scratch" in lib.fds_last_error()
+    scratch = torch.zeros(B * L, 2 * H * 64, dtype=torch.float16, device=cuda_device)
+    rc = lib.fds_rope_attn_fwd_static(ctypes.byref(_args(qkv, cos, sin, out, scratch, B, L, H, status)), None)
+    assert rc == N.FDS_ERR_INVALID_ARGUMENT  # a caller-provided scratch is refused
