@@ -109,8 +109,9 @@ struct Smem {
     static constexpr int kDrain = kPvDone + 2;          // per query tile: its MMA warp's drain
     static constexpr int kNever = kDrain + 2;
     static constexpr int kNumBars = kNever + 1;
+    // misc block: +0 TMEM base, +4 abort flag, +8 status word pointer, +16 wait timeout (ns)
     static constexpr int misc = bars + kNumBars * 8;
-    static constexpr int total = misc + 16;
+    static constexpr int total = misc + 32;
     static constexpr int alloc = total + 1024;  // slack for 1024-byte alignment
 };
 static_assert(Smem::k % 1024 == 0 && Smem::v % 1024 == 0 && Smem::rel % 1024 == 0, "swizzle atoms");
@@ -148,45 +149,53 @@ struct DTypeTraits<__nv_bfloat16> {
     }
 };
 
+// Where the bounded waits find the CTA's abort flag, status word pointer and
+// timeout: the shared-memory misc block (one 32-bit address in registers; the
+// rest is only read on the slow path).
 struct WaitCtl {
-    volatile int* abort;
-    int32_t* status;
-    int64_t timeout_ns;
+    uint32_t misc;
 };
 
-// Wait for completion of phase `parity` of `bar`, for at most ctl.timeout_ns.
-// Returns false (after recording `err_bit` and raising the abort flag) on
-// expiry, or at once when another role has already aborted.
-__device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, const WaitCtl& ctl, int err_bit,
+// Wait for completion of phase `parity` of the mbarrier at shared address
+// `bar`, for at most the CTA's timeout. Returns false (after recording
+// `err_bit` and raising the abort flag) on expiry, or at once when another role
+// has already aborted.
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, WaitCtl ctl, int err_bit,
                                              bool honour_abort = true) {
-    const uint32_t addr = smem_u32(bar);
-    if (mbar_try_wait(addr, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
+    const int64_t timeout_ns = static_cast<int64_t>(ld_shared_u64(ctl.misc + 16));
     const uint64_t t0 = globaltimer_ns();
     // iteration cap: ends the wait even if the global timer were not advancing
     // (each outer round is 16 probes, well over 16 ns)
-    const int64_t max_rounds = ctl.timeout_ns / 16 + 1024;
+    const int64_t max_rounds = timeout_ns / 16 + 1024;
     for (int64_t round = 0;; ++round) {
 #pragma unroll 1
         for (int i = 0; i < 16; ++i)
-            if (mbar_try_wait(addr, parity)) return true;
-        if (honour_abort && *ctl.abort) return false;
-        if (static_cast<int64_t>(globaltimer_ns() - t0) > ctl.timeout_ns || round > max_rounds) {
-            *ctl.abort = 1;
-            if (ctl.status) atomicOr(ctl.status, err_bit);
+            if (mbar_try_wait(bar, parity)) return true;
+        if (honour_abort && ld_shared_volatile_u32(ctl.misc + 4) != 0) return false;
+        if (static_cast<int64_t>(globaltimer_ns() - t0) > timeout_ns || round > max_rounds) {
+            st_shared_volatile_u32(ctl.misc + 4, 1);
+            int* status = reinterpret_cast<int*>(ld_shared_u64(ctl.misc + 8));
+            if (status) atomicOr(status, err_bit);
             return false;
         }
     }
 }
 
-// All 32 lanes wait; the warp proceeds only if every lane saw the phase.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const WaitCtl& ctl, int err_bit) {
+// All 32 lanes wait; the warp proceeds only if every lane saw the phase. Both
+// the first probe and the bounded loop end in a full-warp vote: lanes may reach
+// this point unconverged (after a lane-0-only arrive), and a lane that left
+// early would then sit in the caller's next .sync.aligned tcgen05 instruction
+// while the others wait for it in the vote.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, WaitCtl ctl, int err_bit) {
+    if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
     const bool ok = wait_bounded(bar, parity, ctl, err_bit);
     return __all_sync(0xffffffffu, ok);
 }
 
 // Arrive once per warp on `bar` (initialised with count 4 for a warpgroup):
 // every lane's prior tcgen05 traffic is ordered before the arrival.
-__device__ __forceinline__ void warp_arrive(uint64_t* bar, int lane) {
+__device__ __forceinline__ void warp_arrive(uint32_t bar, int lane) {
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(bar);
@@ -202,9 +211,11 @@ struct TileMma {
     static constexpr uint32_t kIdescPV = idesc_f16(kBlockM, kHeadDim, fmt, 0, 1);
 
     uint8_t* smem;
-    uint64_t* bars;
+    uint32_t bars;  // shared address of the barrier array
     uint32_t tmem;
     int w;  // query tile
+
+    __device__ __forceinline__ uint32_t bar(int idx) const { return bars + 8u * idx; }
 
     __device__ __forceinline__ uint64_t q_desc() const {
         return sw128_desc(smem_u32(smem + (w ? Smem::q1 : Smem::q0)));
@@ -217,7 +228,7 @@ struct TileMma {
 #pragma unroll
             for (int k = 0; k < kHeadDim / 16; ++k)
                 mma_ss(tmem + kTmemS + w * kBlockN, dq + 2 * k, dr + 2 * k, kIdescQR, k > 0);
-            mma_commit(&bars[Smem::kSFull + w]);
+            mma_commit(bar(Smem::kSFull + w));
         }
         __syncwarp();
     }
@@ -230,8 +241,8 @@ struct TileMma {
 #pragma unroll
             for (int k = 0; k < kHeadDim / 16; ++k)
                 mma_ss(tmem + kTmemS + w * kBlockN, dq + 2 * k, dk + 2 * k, kIdescQK, k > 0);
-            mma_commit(&bars[Smem::kSFull + w]);
-            mma_commit(&bars[Smem::kKEmpty + st]);
+            mma_commit(bar(Smem::kSFull + w));
+            mma_commit(bar(Smem::kKEmpty + st));
         }
         __syncwarp();
     }
@@ -244,17 +255,17 @@ struct TileMma {
             for (int k = 0; k < kBlockN / 16; ++k)
                 mma_ts(tmem + kTmemO + w * kHeadDim, tmem + kTmemP + w * (kBlockN / 2) + 8 * k, dv + 128 * k,
                        kIdescPV, (jp > 0 || k > 0) ? 1u : 0u);
-            mma_commit(&bars[Smem::kPvDone + w]);
-            mma_commit(&bars[Smem::kVEmpty + st]);
+            mma_commit(bar(Smem::kPvDone + w));
+            mma_commit(bar(Smem::kVEmpty + st));
         }
         __syncwarp();
     }
 
     // every MMA this lane issued completes before TMEM can be released
-    __device__ __forceinline__ void drain(const WaitCtl& ctl) const {
-        if (elect_one()) mma_commit(&bars[Smem::kDrain + w]);
+    __device__ __forceinline__ void drain(WaitCtl ctl) const {
+        if (elect_one()) mma_commit(bar(Smem::kDrain + w));
         __syncwarp();
-        wait_bounded(&bars[Smem::kDrain + w], 0, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
+        wait_bounded(bar(Smem::kDrain + w), 0, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
         __syncwarp();
     }
 };
@@ -263,16 +274,16 @@ struct TileMma {
 // softmax warps have read S(j) out of TMEM and O += P(j) V(j) once they have
 // stored P(j).
 template <typename T, bool kRelBias>
-__device__ __forceinline__ void mma_role(uint8_t* smem, uint64_t* bars, uint32_t tmem, const WaitCtl& ctl, int w,
+__device__ __forceinline__ void mma_role(uint8_t* smem, uint32_t bars, uint32_t tmem, WaitCtl ctl, int w,
                                          int n_tiles, bool has_q1) {
     if (n_tiles == 0 || (w == 1 && !has_q1)) return;
     const TileMma<T, kRelBias> mma{smem, bars, tmem, w};
     constexpr int err = FDS_STATUS_TIMEOUT_MMA;
-    uint64_t* s_free = &bars[Smem::kSFree + w];
-    uint64_t* p_full = &bars[Smem::kPFull + w];
+    const uint32_t s_free = mma.bar(Smem::kSFree + w);
+    const uint32_t p_full = mma.bar(Smem::kPFull + w);
     uint32_t free_parity = 0;
     bool issued = false;
-    bool ok = warp_wait(&bars[Smem::kQ], 0, ctl, err);
+    bool ok = warp_wait(mma.bar(Smem::kQ), 0, ctl, err);
     if (ok && kRelBias) {
         tc_fence_after();
         mma.qr();
@@ -280,7 +291,7 @@ __device__ __forceinline__ void mma_role(uint8_t* smem, uint64_t* bars, uint32_t
         ok = warp_wait(s_free, free_parity, ctl, err);  // QR copied out of the S columns
         free_parity ^= 1;
     }
-    if (ok) ok = warp_wait(&bars[Smem::kKFull + 0], 0, ctl, err);
+    if (ok) ok = warp_wait(mma.bar(Smem::kKFull + 0), 0, ctl, err);
     if (ok) {
         tc_fence_after();
         mma.s(0);
@@ -290,13 +301,13 @@ __device__ __forceinline__ void mma_role(uint8_t* smem, uint64_t* bars, uint32_t
         if (j + 1 < n_tiles) {
             ok = warp_wait(s_free, free_parity, ctl, err);
             free_parity ^= 1;
-            if (ok) ok = warp_wait(&bars[Smem::kKFull + (j + 1) % kStages], ((j + 1) / kStages) & 1, ctl, err);
+            if (ok) ok = warp_wait(mma.bar(Smem::kKFull + (j + 1) % kStages), ((j + 1) / kStages) & 1, ctl, err);
             if (!ok) break;
             tc_fence_after();
             mma.s(j + 1);
         }
         ok = warp_wait(p_full, j & 1, ctl, err);
-        if (ok) ok = warp_wait(&bars[Smem::kVFull + j % kStages], (j / kStages) & 1, ctl, err);
+        if (ok) ok = warp_wait(mma.bar(Smem::kVFull + j % kStages), (j / kStages) & 1, ctl, err);
         if (!ok) break;
         tc_fence_after();
         mma.pv(j);
@@ -304,10 +315,141 @@ __device__ __forceinline__ void mma_role(uint8_t* smem, uint64_t* bars, uint32_t
     if (issued) mma.drain(ctl);
 }
 
+// O *= alpha for this thread's row (32 lanes of a warp, 64 columns). Rare (the
+// running max moves by more than the lazy threshold), so it is kept out of line:
+// its registers then never compete with the exponentials of the hot loop.
+__device__ __noinline__ void rescale_o_row(uint32_t tO, float alpha) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        uint32_t o[32];
+        tmem_ld32(tO + 32 * half, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+        tmem_st32(tO + 32 * half, o);
+    }
+}
+
+// Online softmax of one query row (this thread) over the KV tiles: per tile,
+// read S out of TMEM, bias, max, exponentiate into P (TMEM), rescale O when the
+// running max moves. One instance per softmax thread; step() handles tile j.
 template <typename T, bool kRelBias>
-__device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint32_t tmem, const AttnParams& p,
-                                             const WaitCtl& ctl, int warp, int lane, int b, int h, int q_base,
-                                             int kv_end, int n_tiles, bool has_q1) {
+struct RowSoftmax {
+    static constexpr int err = FDS_STATUS_TIMEOUT_SOFTMAX;
+    uint32_t tS, tP, tO;
+    float sl;
+    uint32_t qrow;  // shared address of this row's Q.rel^T in log2 units (encoder)
+    uint32_t s_full, s_free, p_full, pv_done;  // barrier shared addresses
+    WaitCtl ctl;
+    int i, kv_end, lane;
+    float m_run, l_run;
+    uint32_t s_parity;
+
+    // kBand: per-score relative bias gathered from qrow (any tile; needed for
+    // the near-diagonal ones); otherwise the per-row constant cb (a tile whose
+    // every pair saturates the clamp, or no bias). kMask: keys >= kv_end.
+    template <bool kBand, bool kMask>
+    __device__ __forceinline__ bool step(int j, float cb) {
+        bool ok = warp_wait(s_full, s_parity, ctl, err);
+        s_parity ^= 1;
+        if (!ok) return false;
+        tc_fence_after();
+
+        uint32_t sr[128];
+        tmem_ld64(tS + 0, *reinterpret_cast<uint32_t(*)[64]>(&sr[0]));
+        tmem_ld64(tS + 64, *reinterpret_cast<uint32_t(*)[64]>(&sr[64]));
+        tmem_wait_ld();
+        warp_arrive(s_free, lane);  // the MMA warp may now compute S(j+1) into these columns
+        float s[128];
+#pragma unroll
+        for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sr[c]);
+
+        const int n0 = j * kBlockN;
+        // score in log2 units = s * mult + cb
+        float mult = sl;
+        if constexpr (kBand) {
+            const int d0 = n0 - i + kClampLeft;
+#pragma unroll
+            for (int c = 0; c < 128; ++c) {
+                const int idx = min(max(d0 + c, 0), kClampLeft + kClampRight);
+                s[c] = fmaf(s[c], sl, ld_shared_f32(qrow + 4u * idx));
+            }
+            mult = 1.f;
+            cb = 0.f;
+        }
+        if constexpr (kMask) {
+            const int lim = kv_end - n0;
+#pragma unroll
+            for (int c = 0; c < 128; ++c)
+                if (c >= lim) s[c] = -INFINITY;
+        }
+
+        float mx[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mx[u] = fmax3(s[u], s[8 + u], s[16 + u]);
+#pragma unroll
+        for (int c = 24; c < 120; c += 16) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) mx[u] = fmax3(mx[u], s[c + u], s[c + 8 + u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mx[u] = fmaxf(mx[u], s[120 + u]);
+        const float mxa = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+        const float tile_max = fmaf(mxa, mult, cb);
+
+        const bool rescale = tile_max > m_run + kRescaleThreshold;
+        float alpha = 1.f;
+        if (rescale) {
+            alpha = ex2_approx(m_run - tile_max);  // 0 on the first tile
+            m_run = tile_max;
+        }
+        const float add = cb - m_run;
+        const float ky = mult * (1.0f / kPolySpan), kb = (add - kPolyLo) * (1.0f / kPolySpan);
+
+        // exponentials into packed 16-bit pairs, held in registers; 3 of every
+        // 10 pairs go through the FMA-pipe polynomial so that the MUFU and FMA
+        // pipes carry similar loads
+        uint32_t pk[64];
+        float2 ls[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) ls[a] = make_float2(0.f, 0.f);
+        const float2 mult2 = make_float2(mult, mult), add2 = make_float2(add, add);
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+            float2 pp;
+            if (c % 10 == 1 || c % 10 == 4 || c % 10 == 7) {
+                pp = exp2_poly2(s[2 * c], s[2 * c + 1], ky, kb);
+            } else {
+                const float2 x = ffma2(make_float2(s[2 * c], s[2 * c + 1]), mult2, add2);
+                pp.x = ex2_approx(x.x);
+                pp.y = ex2_approx(x.y);
+            }
+            ls[c & 3] = fadd2(ls[c & 3], pp);
+            pk[c] = DTypeTraits<T>::pack(pp.x, pp.y);
+        }
+        ls[0] = fadd2(fadd2(ls[0], ls[1]), fadd2(ls[2], ls[3]));
+        l_run = l_run * alpha + (ls[0].x + ls[0].y);
+
+        if (j > 0) {
+            // P(j-1) V(j-1) must be complete before its P columns are rewritten
+            // and before O is rescaled (its latency hides under the work above).
+            ok = warp_wait(pv_done, (j - 1) & 1, ctl, err);
+            if (!ok) return false;
+            tc_fence_after();
+        }
+        tmem_st32(tP + 0, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+        tmem_st32(tP + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
+        if (j > 0 && __any_sync(0xffffffffu, rescale)) rescale_o_row(tO, alpha);
+        tmem_wait_st();
+        warp_arrive(p_full, lane);
+        return true;
+    }
+};
+
+template <typename T, bool kRelBias>
+__device__ __forceinline__ void softmax_role(uint32_t sbase, uint32_t tmem, const AttnParams& p, WaitCtl ctl,
+                                             int warp, int lane, int b, int h, int q_base, int kv_end, int n_tiles,
+                                             bool has_q1) {
     const int wg = (warp - kSoftmaxWarp0) >> 2;  // query tile of this warpgroup
     const int wq = warp & 3;                     // warp within the warpgroup (= TMEM lane quarter)
     const int row = (wq << 5) + lane;            // row in tile == TMEM lane
@@ -327,158 +469,81 @@ __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint
 
     constexpr int err = FDS_STATUS_TIMEOUT_SOFTMAX;
     const uint32_t lane_addr = static_cast<uint32_t>(wq * 32) << 16;
-    const uint32_t tS = tmem + lane_addr + kTmemS + wg * kBlockN;
-    const uint32_t tP = tmem + lane_addr + kTmemP + wg * (kBlockN / 2);
-    const uint32_t tO = tmem + lane_addr + kTmemO + wg * kHeadDim;
+    RowSoftmax<T, kRelBias> rs;
+    rs.tS = tmem + lane_addr + kTmemS + wg * kBlockN;
+    rs.tP = tmem + lane_addr + kTmemP + wg * (kBlockN / 2);
+    rs.tO = tmem + lane_addr + kTmemO + wg * kHeadDim;
+    rs.sl = p.scale_log2;
+    const uint32_t qrow = sbase + Smem::qr + 4u * ((wg * kBlockM + row) * kQrStride);
+    rs.qrow = qrow;
+    const uint32_t bars = sbase + Smem::bars;
+    rs.s_full = bars + 8u * (Smem::kSFull + wg);
+    rs.s_free = bars + 8u * (Smem::kSFree + wg);
+    rs.p_full = bars + 8u * (Smem::kPFull + wg);
+    rs.pv_done = bars + 8u * (Smem::kPvDone + wg);
+    rs.ctl = ctl;
+    rs.i = i;
+    rs.kv_end = kv_end;
+    rs.lane = lane;
+    rs.m_run = -INFINITY;
+    rs.l_run = 0.f;
+    rs.s_parity = 0;
     const float sl = p.scale_log2;
-    float* qrow = reinterpret_cast<float*>(smem + Smem::qr) + (wg * kBlockM + row) * kQrStride;
-    uint64_t* s_full = &bars[Smem::kSFull + wg];
-    uint64_t* s_free = &bars[Smem::kSFree + wg];
-    uint64_t* p_full = &bars[Smem::kPFull + wg];
-    uint64_t* pv_done = &bars[Smem::kPvDone + wg];
 
     bool ok = true;
-    uint32_t s_parity = 0;      // next s_full phase
     float qr_left = 0.f, qr_right = 0.f;
-
     if constexpr (kRelBias) {
-        ok = warp_wait(s_full, s_parity, ctl, err);
-        s_parity ^= 1;
+        ok = warp_wait(rs.s_full, rs.s_parity, ctl, err);
+        rs.s_parity ^= 1;
         if (ok) {
             tc_fence_after();
             uint32_t a[32], c2[32], d[16];
-            tmem_ld32(tS, a);
-            tmem_ld32(tS + 32, c2);
-            tmem_ld16(tS + 64, d);
+            tmem_ld32(rs.tS, a);
+            tmem_ld32(rs.tS + 32, c2);
+            tmem_ld16(rs.tS + 64, d);
             tmem_wait_ld();
-            warp_arrive(s_free, lane);  // the S columns may now receive S(0)
+            warp_arrive(rs.s_free, lane);  // the S columns may now receive S(0)
 #pragma unroll
-            for (int c = 0; c < 32; ++c) qrow[c] = __uint_as_float(a[c]) * sl;
+            for (int c = 0; c < 32; ++c) st_shared_f32(qrow + 4u * c, __uint_as_float(a[c]) * sl);
 #pragma unroll
-            for (int c = 0; c < 32; ++c) qrow[32 + c] = __uint_as_float(c2[c]) * sl;
+            for (int c = 0; c < 32; ++c) st_shared_f32(qrow + 4u * (32 + c), __uint_as_float(c2[c]) * sl);
 #pragma unroll
-            for (int c = 0; c < kNumPos - 64; ++c) qrow[64 + c] = __uint_as_float(d[c]) * sl;
+            for (int c = 0; c < kNumPos - 64; ++c) st_shared_f32(qrow + 4u * (64 + c), __uint_as_float(d[c]) * sl);
             qr_left = __uint_as_float(a[0]) * sl;
             qr_right = __uint_as_float(d[kNumPos - 1 - 64]) * sl;
         }
     }
 
-    const int t0 = q_base + wg * kBlockM;  // first query row of this tile
-    float m_run = -INFINITY;
-    float l_run = 0.f;
-    for (int j = 0; ok && j < n_tiles; ++j) {
-        ok = warp_wait(s_full, s_parity, ctl, err);
-        s_parity ^= 1;
-        if (!ok) break;
-        tc_fence_after();
-
-        uint32_t sr[128];
-        tmem_ld32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-        tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-        tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
-        tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
-        tmem_wait_ld();
-        warp_arrive(s_free, lane);  // the MMA warp may now compute S(j+1) into these columns
-        float s[128];
-#pragma unroll
-        for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sr[c]);
-
-        const int n0 = j * kBlockN;
-        // tile class (uniform over the warpgroup): every pair left-saturated,
-        // every pair right-saturated, or near-diagonal (per-score gather)
-        const bool far_left = (n0 + kBlockN - 1) - t0 <= -kClampLeft;
-        const bool far_right = n0 - (t0 + kBlockM - 1) >= kClampRight;
-        const bool band = kRelBias && !far_left && !far_right;
-        if (band) {
-            const int d0 = n0 - i + kClampLeft;
-#pragma unroll
-            for (int c = 0; c < 128; ++c) {
-                const int idx = min(max(d0 + c, 0), kClampLeft + kClampRight);
-                s[c] = fmaf(s[c], sl, qrow[idx]);
-            }
-        }
-        if (n0 + kBlockN > kv_end) {
-            const int lim = kv_end - n0;
-#pragma unroll
-            for (int c = 0; c < 128; ++c)
-                if (c >= lim) s[c] = -INFINITY;
-        }
-        float mx[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) mx[u] = s[u];
-#pragma unroll
-        for (int c = 8; c < 128; c += 16) {
-#pragma unroll
-            for (int u = 0; u < 8; ++u) mx[u] = fmax3(mx[u], s[c + u], s[c + 8 + u]);
-        }
-        const float mxa = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
-        float cb = 0.f;
-        if constexpr (kRelBias) cb = far_left ? qr_left : qr_right;
-        const float tile_max = band ? mxa : fmaf(mxa, sl, cb);
-
-        const bool rescale = tile_max > m_run + kRescaleThreshold;
-        float alpha = 1.f;
-        if (rescale) {
-            alpha = ex2_approx(m_run - tile_max);  // 0 on the first tile
-            m_run = tile_max;
-        }
-        const float mult = band ? 1.f : sl;
-        const float add = (band ? 0.f : cb) - m_run;
-
-        // exponentials into packed 16-bit pairs, held in registers; 2 of every
-        // 5 pairs go through the FMA-pipe polynomial so that the MUFU and FMA
-        // pipes carry similar loads
-        uint32_t pk[64];
-        float2 ls[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-        const float2 mult2 = make_float2(mult, mult), add2 = make_float2(add, add);
-#pragma unroll
-        for (int c = 0; c < 64; ++c) {
-            const float2 x = ffma2(make_float2(s[2 * c], s[2 * c + 1]), mult2, add2);
-            float2 pp;
-            if (c % 5 == 1 || c % 5 == 3) {
-                pp = exp2_poly2(x);
-            } else {
-                pp.x = ex2_approx(x.x);
-                pp.y = ex2_approx(x.y);
-            }
-            ls[c & 1] = fadd2(ls[c & 1], pp);
-            pk[c] = DTypeTraits<T>::pack(pp.x, pp.y);
-        }
-        l_run = l_run * alpha + ((ls[0].x + ls[0].y) + (ls[1].x + ls[1].y));
-
-        if (j > 0) {
-            // P(j-1) V(j-1) must be complete before its P columns are rewritten
-            // and before O is rescaled (its latency hides under the work above).
-            ok = warp_wait(pv_done, (j - 1) & 1, ctl, err);
-            if (!ok) break;
-            tc_fence_after();
-        }
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) tmem_st16(tP + ch * 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[ch * 16]));
-        if (j > 0 && __any_sync(0xffffffffu, rescale)) {
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                uint32_t o[32];
-                tmem_ld32(tO + 32 * half, o);
-                tmem_wait_ld();
-#pragma unroll
-                for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-                tmem_st32(tO + 32 * half, o);
-            }
-        }
-        tmem_wait_st();
-        warp_arrive(p_full, lane);
+    // Tiles in key order: [0, jb0) every pair left-saturated (bias QR[i,0]),
+    // [jb0, jb1) near-diagonal (per-score gather), [jb1, ...) every pair
+    // right-saturated (bias QR[i,72]). With t0 the tile's first query row, a KV
+    // tile starting at key n0 is near-diagonal iff t0 - 190 <= n0 <= t0 + 134.
+    // Each class runs its own copy of the tile step, so the hot loops carry no
+    // gather code; the last tile (key padding) takes the general step.
+    const int n_last = n_tiles - 1;
+    int j = 0;
+    if constexpr (kRelBias) {
+        const int t0 = q_base + wg * kBlockM;
+        const int jb0 = t0 >= 190 ? (t0 - 190 + kBlockN - 1) / kBlockN : 0;
+        const int jb1 = (t0 + 135 + kBlockN - 1) / kBlockN;
+        for (; ok && j < min(jb0, n_last); ++j) ok = rs.template step<false, false>(j, qr_left);
+        for (; ok && j < min(jb1, n_last); ++j) ok = rs.template step<true, false>(j, 0.f);
+        for (; ok && j < n_last; ++j) ok = rs.template step<false, false>(j, qr_right);
+        if (ok) ok = rs.template step<true, true>(n_last, 0.f);
+    } else {
+        for (; ok && j < n_last; ++j) ok = rs.template step<false, false>(j, 0.f);
+        if (ok) ok = rs.template step<false, true>(n_last, 0.f);
     }
 
-    if (ok) ok = warp_wait(pv_done, (n_tiles - 1) & 1, ctl, err);
+    if (ok) ok = warp_wait(rs.pv_done, (n_tiles - 1) & 1, ctl, err);
     if (ok) {
         tc_fence_after();
         uint32_t o[64];
-        tmem_ld32(tO, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
-        tmem_ld32(tO + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+        tmem_ld32(rs.tO, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+        tmem_ld32(rs.tO + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
         tmem_wait_ld();
         if (i < L) {
-            const float inv = 1.f / l_run;
+            const float inv = 1.f / rs.l_run;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
                 uint4 v;
@@ -495,9 +560,10 @@ __device__ __forceinline__ void softmax_role(uint8_t* smem, uint64_t* bars, uint
 template <bool kRelBias>
 __device__ __forceinline__ void load_role(uint8_t* smem, uint64_t* bars, const CUtensorMap* map_q,
                                           const CUtensorMap* map_k, const CUtensorMap* map_v,
-                                          const CUtensorMap* map_r, const AttnParams& p, const WaitCtl& ctl,
+                                          const CUtensorMap* map_r, const AttnParams& p, WaitCtl ctl,
                                           int b, int h, int q_base, int n_tiles, bool has_q1) {
     if (n_tiles == 0) return;
+    const auto bar = [&](int idx) { return smem_u32(&bars[idx]); };
     if (elect_one()) {
         const uint32_t q_bytes = (has_q1 ? 2 : 1) * kTileBytes + (kRelBias ? kRelRows * 128 : 0);
         mbar_arrive_expect_tx(&bars[Smem::kQ], q_bytes);
@@ -514,7 +580,7 @@ __device__ __forceinline__ void load_role(uint8_t* smem, uint64_t* bars, const C
         const int st = j % kStages;
         const uint32_t par = ((j / kStages) - 1) & 1;
         if (j >= kStages) {
-            ok = warp_wait(&bars[Smem::kKEmpty + st], par, ctl, FDS_STATUS_TIMEOUT_LOAD);
+            ok = warp_wait(bar(Smem::kKEmpty + st), par, ctl, FDS_STATUS_TIMEOUT_LOAD);
             if (!ok) break;
         }
         if (elect_one()) {
@@ -524,10 +590,10 @@ __device__ __forceinline__ void load_role(uint8_t* smem, uint64_t* bars, const C
         }
         __syncwarp();
         if (j >= kStages) {
-            ok = warp_wait(&bars[Smem::kVEmpty + st], par, ctl, FDS_STATUS_TIMEOUT_LOAD);
+            ok = warp_wait(bar(Smem::kVEmpty + st), par, ctl, FDS_STATUS_TIMEOUT_LOAD);
             if (!ok) {
                 // K(j) was issued but V(j) was not: drain K(j) here
-                wait_bounded(&bars[Smem::kKFull + st], (j / kStages) & 1, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
+                wait_bounded(bar(Smem::kKFull + st), (j / kStages) & 1, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
                 break;
             }
         }
@@ -541,13 +607,13 @@ __device__ __forceinline__ void load_role(uint8_t* smem, uint64_t* bars, const C
     }
     if (!ok) {
         // aborted: let every copy already issued land before the CTA exits
-        wait_bounded(&bars[Smem::kQ], 0, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
+        wait_bounded(bar(Smem::kQ), 0, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
         for (int s = 0; s < kStages; ++s) {
             // loads issued into stage s: tiles s, s + kStages, ... below issued_tiles
             const int n = issued_tiles > s ? (issued_tiles - s + kStages - 1) / kStages : 0;
             if (n == 0) continue;
-            wait_bounded(&bars[Smem::kKFull + s], (n - 1) & 1, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
-            wait_bounded(&bars[Smem::kVFull + s], (n - 1) & 1, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
+            wait_bounded(bar(Smem::kKFull + s), (n - 1) & 1, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
+            wait_bounded(bar(Smem::kVFull + s), (n - 1) & 1, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
         }
         __syncwarp();
     }
@@ -559,10 +625,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_r,
                     const AttnParams p) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned base (the swizzle atoms), as an offset into the shared
+    // array so that every access derived from it stays a shared-window access
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    const uint32_t sbase = (raw_addr + 1023u) & ~1023u;
+    uint8_t* smem = smem_raw + (sbase - raw_addr);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Smem::bars);
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + Smem::misc);
-    int* abort_flag = reinterpret_cast<int*>(smem + Smem::misc + 4);
+    const WaitCtl ctl{sbase + Smem::misc};
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -592,7 +662,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int d = 0; d < 2; ++d) mbar_init(&bars[Smem::kDrain + d], 1);
         mbar_init(&bars[Smem::kNever], 1);
-        *abort_flag = 0;
+        st_shared_volatile_u32(ctl.misc + 4, 0);  // abort flag
+        st_shared_u64(ctl.misc + 8, reinterpret_cast<uint64_t>(p.status));
+        st_shared_u64(ctl.misc + 16, static_cast<uint64_t>(p.timeout_ns > 0 ? p.timeout_ns : kDefaultTimeoutNs));
         fence_barrier_init();
         fence_proxy_async_smem();
     }
@@ -610,14 +682,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
-    const WaitCtl ctl{abort_flag, p.status, p.timeout_ns > 0 ? p.timeout_ns : kDefaultTimeoutNs};
 
     // The two register classes never share code again: each branch ends with
     // its own arrival on the CTA-wide barrier (every thread of the CTA arrives
     // exactly once, so all roles have finished with TMEM when it opens).
     if (warp >= kSoftmaxWarp0) {
         setmaxnreg_inc<kSoftmaxRegs>();
-        softmax_role<T, kRelBias>(smem, bars, tmem, p, ctl, warp, lane, b, h, q_base, kv_end, n_tiles, has_q1);
+        softmax_role<T, kRelBias>(sbase, tmem, p, ctl, warp, lane, b, h, q_base, kv_end, n_tiles, has_q1);
         __syncwarp();
         tc_fence_before();
         named_barrier_sync(1, kThreads);
@@ -628,8 +699,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             // the bounded-wait error path without a real hang
             bool go = true;
             if (p.debug_flags & FDS_DEBUG_FORCE_TIMEOUT)
-                go = warp_wait(&bars[Smem::kNever], 0, ctl, FDS_STATUS_TIMEOUT_MMA);
-            if (go) mma_role<T, kRelBias>(smem, bars, tmem, ctl, (warp - kMmaWarp0) >> 1, n_tiles, has_q1);
+                go = warp_wait(sbase + Smem::bars + 8u * Smem::kNever, 0, ctl, FDS_STATUS_TIMEOUT_MMA);
+            if (go)
+                mma_role<T, kRelBias>(smem, sbase + Smem::bars, tmem, ctl, (warp - kMmaWarp0) >> 1, n_tiles, has_q1);
         } else if (warp == kLoadWarp) {
             load_role<kRelBias>(smem, bars, &map_q, &map_k, &map_v, &map_r, p, ctl, b, h, q_base, n_tiles, has_q1);
         }

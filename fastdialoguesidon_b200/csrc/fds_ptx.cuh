@@ -51,6 +51,34 @@ __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t count) 
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// ---------------------------------------------------------------- shared-memory scalars
+// 32-bit shared-window addresses keep these accesses to one register operand.
+
+__device__ __forceinline__ uint32_t ld_shared_volatile_u32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.volatile.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_shared_volatile_u32(uint32_t addr, uint32_t v) {
+    asm volatile("st.volatile.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_shared_u64(uint32_t addr) {
+    uint64_t v;
+    asm volatile("ld.shared.u64 %0, [%1];" : "=l"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_shared_u64(uint32_t addr, uint64_t v) {
+    asm volatile("st.shared.u64 [%0], %1;" ::"r"(addr), "l"(v) : "memory");
+}
+__device__ __forceinline__ float ld_shared_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_shared_f32(uint32_t addr, float v) {
+    asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -65,9 +93,10 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+__device__ __forceinline__ void mbar_arrive(uint32_t bar_addr) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar_addr) : "memory");
 }
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) { mbar_arrive(smem_u32(bar)); }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
@@ -160,9 +189,8 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
 }
 
 // Arrive once on `bar` when every tcgen05 operation issued so far by this thread has completed.
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     smem_u32(bar))
+__device__ __forceinline__ void mma_commit(uint32_t bar_addr) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_addr)
                  : "memory");
 }
 
@@ -181,6 +209,28 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
           "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
           "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+
+// 32 lanes x 32 bit, 64 consecutive columns (one instruction: lower latency
+// than two x32 loads).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+        "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+        "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+          "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+          "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]),
+          "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]),
+          "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]),
+          "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]),
+          "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
         : "r"(taddr)
         : "memory");
 }
@@ -284,20 +334,35 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
-// 2^x for a pair on the FMA pipe (keeps the MUFU free for the other pairs).
-// x = j + f with j = round(x) from the 1.5 * 2^23 shifter (t = x + C holds j
-// in its low mantissa bits, t - C = j exactly), f = x - j in [-1/2, 1/2];
+// Saturating scalar FMA: min(max(a * b + c, 0), 1) with one rounding.
+__device__ __forceinline__ float fma_sat(float a, float b, float c) {
+    float d;
+    asm("fma.rn.sat.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// 2^x for a pair on the FMA pipe (keeps the MUFU free for the other pairs),
+// where x = s * mult + add. The caller passes ky = mult / kPolySpan and
+// kb = (add - kPolyLo) / kPolySpan; a saturating FMA maps s to
+// y = clamp((x - kPolyLo) / kPolySpan, 0, 1), i.e. x is clamped to
+// [kPolyLo, kPolyLo + kPolySpan] = [-126, 66], for every input including
+// -inf and values far above the softmax's range (2^66 is far beyond what the
+// callers accept, so such a tile is always redone with its exact maximum).
+// Then x = j + f with j = round(x) from the 1.5 * 2^23 shifter
+// (t = y * span + (C + lo) holds j in its low mantissa bits, exactly),
+// f = y * span + (C + lo - t) in [-1/2, 1/2] with a single rounding;
 // q(f) ~ 2^f is a cubic minimax fit of the relative error (max 7.5e-5, see
-// fit_exp2_poly.py), and 2^j enters by adding j to q's exponent field. x is
-// clamped to >= -125 so that the exponent field stays normal (2^-125 is
-// indistinguishable from 0 next to the row sum, which is >= 1).
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-    constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
-    x.x = fmaxf(x.x, -125.0f);
-    x.y = fmaxf(x.y, -125.0f);
-    const float2 t = fadd2(x, make_float2(kShift, kShift));
-    const float2 r = fadd2(t, make_float2(-kShift, -kShift));
-    const float2 f = fadd2(x, make_float2(-r.x, -r.y));
+// fit_exp2_poly.py), and 2^j enters by adding j to q's exponent field, which
+// stays in range for j in [-126, 66].
+constexpr float kPolyLo = -126.0f;
+constexpr float kPolySpan = 192.0f;
+__device__ __forceinline__ float2 exp2_poly2(float s0, float s1, float ky, float kb) {
+    constexpr float kShiftLo = 12582912.0f + kPolyLo;  // 1.5 * 2^23 - 126, exact
+    const float2 y = make_float2(fma_sat(s0, ky, kb), fma_sat(s1, ky, kb));
+    const float2 span = make_float2(kPolySpan, kPolySpan), shift = make_float2(kShiftLo, kShiftLo);
+    const float2 t = ffma2(y, span, shift);                       // C + round(x)
+    const float2 r = ffma2(t, make_float2(-1.f, -1.f), shift);    // -126 - j (exact)
+    const float2 f = ffma2(y, span, r);                           // x - j
     float2 q = ffma2(make_float2(0.0551716685295105f, 0.0551716685295105f), f,
                      make_float2(0.2426111251115799f, 0.2426111251115799f));
     q = ffma2(q, f, make_float2(0.6932609677314758f, 0.6932609677314758f));

@@ -91,6 +91,46 @@ def test_full_size_peaky(cuda_device):
     _check(exp, out)
 
 
+def test_rising_scores_redo_path(cuda_device):
+    """Keys whose norm grows along the sequence: later KV tiles exceed the
+    reference max set by the first tile by far more than 2^14, so the kernel's
+    speculative tiles are redone with their exact max (and O rescaled) many
+    times per row, in both 16-bit types."""
+    B, L, H = 1, 1500, 2
+    for dtype in (torch.float16, torch.bfloat16):
+        qkv, rel = _inputs(B, L, H, seed=51, dtype=torch.float32, rel_std=0.1)
+        qkv = qkv.view(L, 3, H, 64)
+        qkv[:, 1] *= torch.linspace(0.2, 6.0, L).view(L, 1, 1)
+        qkv[:, 2] *= 0.5  # context rows of single values: keep them where fp16 rounds finer than 2e-3
+        qkv = qkv.reshape(L, 3 * H * 64).to(dtype)
+        rel = rel.to(dtype)
+        exp = O.flexrel_attention(qkv, B, H, rel)
+        out = F.flexrel_attention(qkv.to(cuda_device), B, H, rel.to(cuda_device))
+        F.check_status()
+        _check(exp, out, dtype)
+
+
+@pytest.mark.parametrize("key", [642, 643, 700])
+def test_score_jump_beyond_exponent_range(cuda_device, key):
+    """One key, in a late tile, scores ~180 (log2 units) above everything the
+    first tile saw: beyond the fp32 exponent range of 2^x, in a column served
+    by the FMA-pipe polynomial (642, 643) or by the MUFU (700). The output row
+    must be that key's value."""
+    B, L, H = 1, 1000, 1
+    qkv, rel = _inputs(B, L, H, seed=61, dtype=torch.float32, std=0.3, rel_std=0.0)
+    qkv = qkv.view(L, 3, H, 64)
+    qkv[:, 0] = 4.0
+    qkv[key, 1] = 4.0
+    qkv = qkv.reshape(L, 3 * H * 64).half()
+    rel = rel.half()
+    exp = O.flexrel_attention(qkv, B, H, rel)
+    out = F.flexrel_attention(qkv.to(cuda_device), B, H, rel.to(cuda_device))
+    F.check_status()
+    _check(exp, out)
+    v_key = qkv.float().view(L, 3, H, 64)[key, 2, 0]
+    assert torch.allclose(out.float().cpu()[:, :64], v_key.expand(L, 64), atol=2e-3)
+
+
 def test_config3_variable_windows(cuda_device):
     """BASELINE config 3 shape: 8 windows U(3.2, 120) s, bucketed to 500 frames,
     key-padding via kv_len (2 heads: heads are independent)."""
