@@ -55,6 +55,11 @@ def parse_args():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-dit", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's own GPU ops (baseline/_ref) beside ours")
+    ap.add_argument("--schedule", choices=("auto", "unit"), default="auto",
+                    help="auto: the library picks whole units per CTA or the balanced (stream-K) grid; "
+                         "unit: always one 256-row unit per CTA")
     ap.add_argument("--case", choices=("enc1", "dit1"), default=None,
                     help="profiling case: W + K eager launches of one layer (encoder or DiT) at L=6000")
     return ap.parse_args()
@@ -204,7 +209,7 @@ def time_graph(fn, steps: int, warmup: int, device: torch.device, dist_on: bool)
     return ms
 
 
-def e2e_encoder(qkvs, rels, steps: int, warmup: int, device: torch.device, dist_on: bool):
+def e2e_encoder(qkvs, rels, steps: int, warmup: int, device: torch.device, dist_on: bool, bal: bool = True):
     """The same metric through the public API with host buffers: every step copies
     its 13 QKV + rel tables host->device (pinned) and the 13 contexts back,
     overlapped over a copy-in / compute / copy-out stream pipeline."""
@@ -234,7 +239,7 @@ def e2e_encoder(qkvs, rels, steps: int, warmup: int, device: torch.device, dist_
                 ev_in[i].record(s_in)
             comp.wait_event(ev_in[i])
             comp.wait_event(ev_out[i])  # dev_out[i] read back by the previous step
-            F.flexrel_attention(dev_in[i], 1, ENC_HEADS, dev_rel[i], out=dev_out[i])
+            F.flexrel_attention(dev_in[i], 1, ENC_HEADS, dev_rel[i], out=dev_out[i], balanced=bal)
             ev_c[i].record(comp)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ev_c[i])
@@ -296,6 +301,67 @@ def cpu_sample_ms_per_window(rows: int = 6000, threads: int | None = None) -> tu
                           f"({dt:.2f} s), scaled x{L / rows:.2f} rows x 13 layers"}
 
 
+def reference_gpu_leg(qkvs, rels, outs, dit_inputs, device, steps: int = 5) -> dict:
+    """The reference's own GPU ops, installed unmodified under baseline/_ref
+    (fds_triton.kernels), timed eagerly with CUDA events on the same window
+    inputs as our arm: its fused Triton kernel and its split path (two causal
+    SDPA calls + band merge, trt/src/fastdialoguesidon/flexrel_triton.py) for the
+    encoder, rope_split + SDPA for the DiT (the reference model's pattern).
+    Reported beside our numbers; never part of our timed region."""
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(path, "fds_triton")):
+        return {"unavailable": "baseline/_ref/fds_triton not installed"}
+    if path not in sys.path:
+        sys.path.insert(0, path)
+    try:
+        import torch.nn.functional as Fn
+        from fds_triton import kernels as RK
+    except Exception as ex:  # noqa: BLE001 - report, do not fail the bench
+        return {"unavailable": f"import failed: {type(ex).__name__}: {str(ex)[:120]}"}
+
+    def timed(fn) -> float:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(device)
+        return e0.elapsed_time(e1) / steps
+
+    res = {"source": "fds_triton.kernels from baseline/_ref (unmodified), eager launches, CUDA events",
+           "steps": steps}
+    for name, op in (("fused", getattr(RK, "flexrel_attention", None)),
+                     ("split", getattr(RK, "flexrel_attention_split", None))):
+        if op is None:
+            continue
+        try:
+            diff = (op(qkvs[0], 1, ENC_HEADS, rels[0]).float() - outs[0].float()).abs().max().item()
+            ms = timed(lambda: [op(q, 1, ENC_HEADS, r) for q, r in zip(qkvs, rels)])
+            res[f"encoder_{name}_ms_per_window"] = round(ms, 4)
+            res[f"encoder_{name}_max_abs_diff_vs_ours"] = diff
+        except Exception as ex:  # noqa: BLE001
+            res[f"encoder_{name}"] = f"failed: {type(ex).__name__}: {str(ex)[:120]}"
+    if dit_inputs is not None and hasattr(RK, "rope_split"):
+        dq, cos, sin, dout = dit_inputs
+        shape = (1, L_WINDOW, DIT_HEADS, HEAD_DIM)
+
+        def ref_dit(q2):
+            q, k, v = RK.rope_split(q2, L_WINDOW, DIT_HEADS, cos, sin)
+            a = Fn.scaled_dot_product_attention(*(t.view(shape).transpose(1, 2) for t in (q, k, v)))
+            return a.transpose(1, 2).reshape(L_WINDOW, DIT_HEADS * HEAD_DIM)
+
+        try:
+            diff = (ref_dit(dq[0]).float() - dout[0].float()).abs().max().item()
+            res["dit_ms_per_window"] = round(timed(lambda: [ref_dit(q) for q in dq]), 4)
+            res["dit_max_abs_diff_vs_ours"] = diff
+        except Exception as ex:  # noqa: BLE001
+            res["dit"] = f"failed: {type(ex).__name__}: {str(ex)[:120]}"
+    return res
+
+
 # ------------------------------------------------------------------ arms
 
 
@@ -338,20 +404,22 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     if dist_on:
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
 
+    bal = args.schedule == "auto"
     qkvs, rels = make_window(seed=1000 + rank, device=device)
     outs = [torch.empty(L_WINDOW, ENC_HEADS * HEAD_DIM, dtype=torch.float16, device=device) for _ in qkvs]
 
     def enc_step():
         for q, r, o in zip(qkvs, rels, outs):
-            F.flexrel_attention(q, 1, ENC_HEADS, r, out=o)
+            F.flexrel_attention(q, 1, ENC_HEADS, r, out=o, balanced=bal)
 
     with ClockSampler(device) as clocks:
         ms = time_graph(enc_step, args.steps, args.warmup, device, dist_on)
     F.check_status(device)
     e2e_steps = max(3, min(args.steps, 60))
-    e2e_ms, h2d, d2h = e2e_encoder(qkvs, rels, e2e_steps, max(3, min(args.warmup, 5)), device, dist_on)
+    e2e_ms, h2d, d2h = e2e_encoder(qkvs, rels, e2e_steps, max(3, min(args.warmup, 5)), device, dist_on, bal)
 
     dit = None
+    dit_inputs = None
     if not args.no_dit:
         dq = []
         gen = torch.Generator(device=device).manual_seed(2000 + rank)
@@ -364,12 +432,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
         def dit_step():
             for q, o in zip(dq, dout):
-                F.rope_attention(q, 1, DIT_HEADS, cos, sin, out=o, scratch=scratch)
+                F.rope_attention(q, 1, DIT_HEADS, cos, sin, out=o, scratch=scratch, balanced=bal)
 
         dsteps = max(3, args.steps // 2)
         dms = time_graph(dit_step, dsteps, args.warmup, device, dist_on)
         F.check_status(device)
         dit = (dms, dsteps)
+        dit_inputs = (dq, cos, sin, dout)
 
     t = torch.tensor([ms, e2e_ms, dit[0] if dit else 0.0], dtype=torch.float64, device=device)
     if dist_on:
@@ -414,6 +483,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             cms, info = cpu_sample_ms_per_window(rows=1024, threads=os.cpu_count())
             line["cpu_baseline"] = {"value": round(cms, 1), "unit": UNIT, "cores": info["cores"],
                                     "kind": "port", "sample": info["sample"]}
+        if world == 1 and not args.no_reference_gpu:
+            line["reference_gpu"] = reference_gpu_leg(qkvs, rels, outs, dit_inputs, device)
         print(json.dumps(line), flush=True)
 
     if dist_on:
@@ -426,18 +497,20 @@ def run_case(args) -> None:
     import fastdialoguesidon_b200 as F
 
     device = torch.device("cuda", 0)
+    bal = args.schedule == "auto"
     gen = torch.Generator(device=device).manual_seed(7)
     if args.case == "enc1":
         qkv = (torch.randn(L_WINDOW, 3 * ENC_HEADS * HEAD_DIM, generator=gen, device=device) * 0.64).half()
         rel = (torch.randn(73, HEAD_DIM, generator=gen, device=device) * 0.02).half()
         out = torch.empty(L_WINDOW, ENC_HEADS * HEAD_DIM, dtype=torch.float16, device=device)
-        fn, flop = (lambda: F.flexrel_attention(qkv, 1, ENC_HEADS, rel, out=out)), FLOP_ENC_LAYER
+        fn, flop = (lambda: F.flexrel_attention(qkv, 1, ENC_HEADS, rel, out=out, balanced=bal)), FLOP_ENC_LAYER
     else:
         qkv = (torch.randn(L_WINDOW, 3 * DIT_HEADS * HEAD_DIM, generator=gen, device=device) * 0.55).half()
         cos, sin = F.rope_tables(L_WINDOW, device)
         out = torch.empty(L_WINDOW, DIT_HEADS * HEAD_DIM, dtype=torch.float16, device=device)
         scratch = torch.empty(L_WINDOW, 2 * DIT_HEADS * HEAD_DIM, dtype=torch.float16, device=device)
-        fn, flop = (lambda: F.rope_attention(qkv, 1, DIT_HEADS, cos, sin, out=out, scratch=scratch)), FLOP_DIT_LAYER
+        fn, flop = (lambda: F.rope_attention(qkv, 1, DIT_HEADS, cos, sin, out=out, scratch=scratch,
+                                             balanced=bal)), FLOP_DIT_LAYER
     for _ in range(args.warmup):
         fn()
     torch.cuda.synchronize(device)

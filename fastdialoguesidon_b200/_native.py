@@ -30,7 +30,7 @@ FDS_DEBUG_FORCE_TIMEOUT = 0x1
 
 FDS_ROPE_STATIC_SCRATCH_BYTES = 20 * 1024 * 1024
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 # every symbol include/fds_b200.h declares (checked by the CPU test suite)
 EXPORTED_SYMBOLS = (
@@ -41,6 +41,8 @@ EXPORTED_SYMBOLS = (
     "fds_abi_version",
     "fds_last_error",
     "fds_attn_smem_bytes",
+    "fds_attn_workspace_bytes",
+    "fds_attn_schedule",
 )
 
 
@@ -61,6 +63,9 @@ class FdsFlexRelArgs(ctypes.Structure):
         ("scale", ctypes.c_float),
         ("timeout_ns", ctypes.c_int64),
         ("debug_flags", ctypes.c_int32),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_int64),
+        ("grid_ctas", ctypes.c_int32),
     ]
 
 
@@ -82,6 +87,9 @@ class FdsRopeArgs(ctypes.Structure):
         ("scale", ctypes.c_float),
         ("timeout_ns", ctypes.c_int64),
         ("debug_flags", ctypes.c_int32),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_int64),
+        ("grid_ctas", ctypes.c_int32),
     ]
 
 
@@ -124,10 +132,25 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         lib.fds_last_error.restype = ctypes.c_char_p
         lib.fds_attn_smem_bytes.argtypes = []
         lib.fds_attn_smem_bytes.restype = ctypes.c_int
+        lib.fds_attn_workspace_bytes.argtypes = [ctypes.c_int32]
+        lib.fds_attn_workspace_bytes.restype = ctypes.c_int64
+        lib.fds_attn_schedule.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                          ctypes.c_int64, ctypes.c_int32, ctypes.POINTER(ctypes.c_int64)]
+        lib.fds_attn_schedule.restype = ctypes.c_int
         if lib.fds_abi_version() != ABI_VERSION:
             raise RuntimeError(f"{path}: ABI version {lib.fds_abi_version()} != {ABI_VERSION}")
         _lib = lib
         return lib
+
+
+def schedule(batch: int, heads: int, seq_len: int, has_kv_len: bool = False, workspace_bytes: int = 0,
+             grid_ctas: int = 0) -> tuple[int, int, int]:
+    """(CTAs, whole-unit CTAs, pieces of the split last wave) of a launch of this shape."""
+    out = (ctypes.c_int64 * 3)()
+    rc = load().fds_attn_schedule(batch, heads, seq_len, int(has_kv_len), workspace_bytes, grid_ctas, out)
+    if rc != FDS_OK:
+        raise RuntimeError(f"fds_attn_schedule failed ({rc}): {last_error()}")
+    return int(out[0]), int(out[1]), int(out[2])
 
 
 def last_error() -> str:

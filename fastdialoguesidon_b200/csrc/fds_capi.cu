@@ -111,14 +111,101 @@ int make_rel_map(CUtensorMap* map, const void* base, int dtype) {
     return FDS_OK;
 }
 
+// SMs of the current device (cached per device); 0 if it cannot be queried.
+int sm_count() {
+    static int cached[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    if (cached[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
+
+// Workspace of the split last wave for up to G pieces: the part counts (one
+// per cut unit and 32-row group; at most G <= kMaxPieces units are cut) in a
+// fixed region, so that calls with different piece counts can share a
+// workspace (the counts stay zero between calls), then G x kMaxItems slots of
+// 256 rows x kPartRowFloats floats.
+constexpr int64_t kMaxPieces = 1024;
+constexpr int64_t kWsSlotsOffset = kMaxPieces * fds::kSoftmaxWarps * 4;
+int64_t ws_bytes_for(int64_t G) {
+    return kWsSlotsOffset + G * fds::kMaxItems * fds::kRowsPerCta * fds::kPartRowFloats * 4;
+}
+
+struct Workspace {
+    void* ptr;
+    int64_t bytes;
+    int grid_ctas;
+};
+
+// How a launch is laid out: `grid` CTAs, the first `whole` of them one unit
+// each, the last `pieces` the cut last wave (0: one unit per CTA).
+struct Plan {
+    int64_t grid, whole, pieces;
+};
+
+// The split last wave needs a workspace, no kv_len, and with G = grid_ctas
+// (0: the SM count) waves = ceil(U / G), the (waves - 1) G whole units first
+// and the remaining units cut by weight into G pieces such that every piece
+// touches at most kMaxItems (3) units and every cut unit has at most kMaxParts
+// (4) parts: the piece weight is between a third of a two-tile unit (and at
+// least one tile) and twice the lightest unit. With grid_ctas == 0 it is used only when whole units leave
+// more than 3% of the SM time of the waves idle.
+Plan plan_schedule(int64_t batch, int64_t heads, int64_t seq_len, bool has_kv_len, bool has_ws, int64_t ws_bytes,
+                   int64_t grid_ctas, int64_t sms) {
+    const int64_t R = (seq_len + fds::kRowsPerCta - 1) / fds::kRowsPerCta;
+    const int64_t U = batch * heads * R;
+    Plan plan{U, U, 0};
+    const int64_t G = grid_ctas > 0 ? grid_ctas : sms;
+    if (!has_ws || has_kv_len || G <= 0 || G > kMaxPieces) return plan;
+    const int64_t waves = (U + G - 1) / G;
+    if (grid_ctas == 0 && static_cast<double>(U) / static_cast<double>(waves * G) >= 0.97) return plan;
+    const int64_t n = (seq_len + fds::kBlockN - 1) / fds::kBlockN;
+    const int64_t w2 = fds::kWeightTwoTiles;
+    const int64_t w_last = (R - 1) * fds::kRowsPerCta + fds::kBlockM < seq_len ? w2 : fds::kWeightOneTile;
+    const int64_t per_bh = n * ((R - 1) * w2 + w_last);
+    const int64_t whole = (waves - 1) * G;
+    const auto unit_pos = [&](int64_t u) { return (u / R) * per_bh + (u % R) * n * w2; };
+    const int64_t total = unit_pos(U);
+    const int64_t wt = total - unit_pos(whole);
+    const int64_t w_min = wt / G, w_max = (wt + G - 1) / G;
+    const bool ok = ws_bytes >= ws_bytes_for(G) && w_min >= w2 && 3 * w_min >= n * w2 && w_max <= 2 * n * w_last &&
+                    G * total < (int64_t{1} << 31);
+    if (ok) plan = Plan{whole + G, whole, G};
+    return plan;
+}
+
+// Launches on `plan`; the workspace is split into counts and slots.
 template <typename T, bool kRelBias>
 int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mr,
-                const fds::AttnParams& p, int batch, cudaStream_t stream) {
+                fds::AttnParams p, int batch, const Workspace& ws, cudaStream_t stream) {
     auto kern = fds::attn_fwd_kernel<T, kRelBias>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fds::Smem::alloc);
     if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    const dim3 grid((p.seq_len + fds::kRowsPerCta - 1) / fds::kRowsPerCta, batch * p.heads);
-    kern<<<grid, fds::kThreads, fds::Smem::alloc, stream>>>(mq, mk, mv, mr, p);
+    p.row_blocks = (p.seq_len + fds::kRowsPerCta - 1) / fds::kRowsPerCta;
+    const int64_t U = static_cast<int64_t>(batch) * p.heads * p.row_blocks;
+    if (U > 0x7fffffffLL) return fail(FDS_ERR_INVALID_ARGUMENT, "too many work units (%lld)", static_cast<long long>(U));
+    const int sms = sm_count();
+    if (ws.grid_ctas < 0 || (ws.grid_ctas > 0 && sms > 0 && ws.grid_ctas > sms))
+        return fail(FDS_ERR_INVALID_ARGUMENT, "grid_ctas must be in [0, %d] (got %d)", sms, ws.grid_ctas);
+    if (ws.ptr != nullptr && (reinterpret_cast<uintptr_t>(ws.ptr) & 255u) != 0)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+    const Plan plan = plan_schedule(batch, p.heads, p.seq_len, p.kv_len != nullptr, ws.ptr != nullptr, ws.bytes,
+                                    ws.grid_ctas, sms);
+    p.n_units = static_cast<int32_t>(U);
+    p.whole_ctas = static_cast<int32_t>(plan.whole);
+    p.pieces = static_cast<int32_t>(plan.pieces);
+    p.parts = nullptr;
+    p.counts = nullptr;
+    if (plan.pieces > 0) {
+        char* base = static_cast<char*>(ws.ptr);
+        p.counts = reinterpret_cast<uint32_t*>(base);
+        p.parts = reinterpret_cast<float*>(base + kWsSlotsOffset);
+    }
+    kern<<<static_cast<unsigned>(plan.grid), fds::kThreads, fds::Smem::alloc, stream>>>(mq, mk, mv, mr, p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
     return FDS_OK;
@@ -172,6 +259,35 @@ const char* fds_last_error(void) { return g_last_error.c_str(); }
 
 int fds_attn_smem_bytes(void) { return fds::Smem::alloc; }
 
+int64_t fds_attn_workspace_bytes(int32_t grid_ctas) {
+    int64_t G = grid_ctas;
+    if (G <= 0) {
+        G = sm_count();
+        if (G <= 0) {
+            fail(FDS_ERR_CUDA, "cannot query the SM count of the current device");
+            return 0;
+        }
+    }
+    return ws_bytes_for(G);
+}
+
+int fds_attn_schedule(int32_t batch, int32_t heads, int32_t seq_len, int32_t has_kv_len, int64_t workspace_bytes,
+                      int32_t grid_ctas, int64_t* out) {
+    if (out == nullptr || batch < 1 || heads < 1 || seq_len < 1 || grid_ctas < 0)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "fds_attn_schedule: invalid arguments");
+    int64_t sms = 0;
+    if (grid_ctas == 0 && workspace_bytes > 0) {
+        sms = sm_count();
+        if (sms <= 0) return fail(FDS_ERR_CUDA, "cannot query the SM count of the current device");
+    }
+    const Plan plan = plan_schedule(batch, heads, seq_len, has_kv_len != 0, workspace_bytes > 0, workspace_bytes,
+                                    grid_ctas, sms);
+    out[0] = plan.grid;
+    out[1] = plan.whole;
+    out[2] = plan.pieces;
+    return ok();
+}
+
 int fds_flexrel_attn_fwd(const FdsFlexRelArgs* a, void* stream) {
     if (a == nullptr) return fail(FDS_ERR_INVALID_ARGUMENT, "null args");
     int rc = check_common(a->qkv, a->qkv_row_stride, a->out, a->out_row_stride, a->batch, a->heads, a->seq_len,
@@ -203,8 +319,9 @@ int fds_flexrel_attn_fwd(const FdsFlexRelArgs* a, void* stream) {
     p.scale_log2 = a->scale * 1.4426950408889634f;
     p.debug_flags = a->debug_flags;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    rc = a->dtype == FDS_DTYPE_FP16 ? launch_attn<__half, true>(mqkv, mqkv, mqkv, mrel, p, a->batch, s)
-                                    : launch_attn<__nv_bfloat16, true>(mqkv, mqkv, mqkv, mrel, p, a->batch, s);
+    const Workspace ws{a->workspace, a->workspace_bytes, a->grid_ctas};
+    rc = a->dtype == FDS_DTYPE_FP16 ? launch_attn<__half, true>(mqkv, mqkv, mqkv, mrel, p, a->batch, ws, s)
+                                    : launch_attn<__nv_bfloat16, true>(mqkv, mqkv, mqkv, mrel, p, a->batch, ws, s);
     return rc == FDS_OK ? ok() : rc;
 }
 
@@ -270,8 +387,9 @@ int fds_rope_attn_fwd(const FdsRopeArgs* a, void* stream) {
     p.v_x0 = static_cast<int32_t>(2 * hid);
     p.scale_log2 = a->scale * 1.4426950408889634f;
     p.debug_flags = a->debug_flags;
-    rc = a->dtype == FDS_DTYPE_FP16 ? launch_attn<__half, false>(mqk, mqk, mv, mqk, p, a->batch, s)
-                                    : launch_attn<__nv_bfloat16, false>(mqk, mqk, mv, mqk, p, a->batch, s);
+    const Workspace ws{a->workspace, a->workspace_bytes, a->grid_ctas};
+    rc = a->dtype == FDS_DTYPE_FP16 ? launch_attn<__half, false>(mqk, mqk, mv, mqk, p, a->batch, ws, s)
+                                    : launch_attn<__nv_bfloat16, false>(mqk, mqk, mv, mqk, p, a->batch, ws, s);
     return rc == FDS_OK ? ok() : rc;
 }
 

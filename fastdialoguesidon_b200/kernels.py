@@ -8,6 +8,15 @@ dispatch), no autotuning, no host synchronisation and no allocation other than
 ``out`` (and the DiT's rotated-q|k scratch), so every call is safe inside
 ``torch.cuda.graph`` capture once the device has run one eager call.
 
+Schedule: each (device, stream) gets one zero-filled workspace (about 20 MB on
+a 148-SM B200, created on its first call there) that lets the library split
+the last wave -- when whole 256-row units would leave part of it idle, its
+units are cut into one piece per SM and the parts merged through the
+workspace. Calls on one stream are ordered, so they share it safely; a
+workspace created during graph capture belongs to the graph's memory pool and
+is zero-filled by a node of that graph. After a reported timeout
+(:func:`check_status`) the device's workspaces are zero-filled again.
+
 Errors: invalid arguments raise :class:`FdsError` before any launch. It
 subclasses both ``AssertionError`` (what the reference's ``assert`` checks
 raise, ``kernels.py:430, 641``) and ``RuntimeError``. A missing native library
@@ -36,6 +45,7 @@ class FdsError(AssertionError, RuntimeError):
 
 _DTYPES = {torch.float16: N.FDS_DTYPE_FP16, torch.bfloat16: N.FDS_DTYPE_BF16}
 _status_words: dict[int, torch.Tensor] = {}
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
 
 
 def _check(cond: bool, msg: str) -> None:
@@ -63,6 +73,9 @@ def check_status(device: torch.device | int | None = None, clear: bool = True) -
     bits = int(st[0].item())
     if clear and bits:
         st.zero_()
+        for (idx, _), ws in _workspaces.items():
+            if idx == dev.index:
+                ws.zero_()  # an aborted split may leave part counts behind
     if bits:
         raise FdsError(f"FDS kernel on {dev} reported a bounded-wait timeout (status bits 0x{bits:x})")
     return bits
@@ -70,6 +83,29 @@ def check_status(device: torch.device | int | None = None, clear: bool = True) -
 
 def _stream_ptr(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def _workspace(device: torch.device, lib) -> tuple[int, int]:
+    """(pointer, bytes) of the balanced-schedule workspace of ``device``'s
+    current stream; the C library leaves it ready for the next call."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, _stream_ptr(device))
+    ws = _workspaces.get(key)
+    if ws is None:
+        nbytes = int(lib.fds_attn_workspace_bytes(0))
+        if nbytes <= 0:
+            raise FdsError(f"fds_attn_workspace_bytes failed: {N.last_error()}")
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
+        _workspaces[key] = ws
+    return ws.data_ptr(), ws.numel()
+
+
+def _schedule(device: torch.device, lib, balanced: bool, grid_ctas: int) -> dict:
+    _check(grid_ctas >= 0, "grid_ctas must be >= 0")
+    if not balanced:
+        return dict(workspace=None, workspace_bytes=0, grid_ctas=0)
+    ptr, nbytes = _workspace(device, lib)
+    return dict(workspace=ptr, workspace_bytes=nbytes, grid_ctas=int(grid_ctas))
 
 
 def _rows_operand(t: torch.Tensor, name: str) -> None:
@@ -93,7 +129,8 @@ def _raise_rc(rc: int, what: str) -> None:
 
 def flexrel_attention(qkv: torch.Tensor, batch: int, heads: int, rel: torch.Tensor,
                       out: torch.Tensor | None = None, kv_len: torch.Tensor | None = None,
-                      *, timeout_ns: int = 0, debug_flags: int = 0) -> torch.Tensor:
+                      *, timeout_ns: int = 0, debug_flags: int = 0, balanced: bool = True,
+                      grid_ctas: int = 0) -> torch.Tensor:
     """Relative-key self-attention of one w2v-BERT layer.
 
     qkv [B*L, 3*H*64] fp16/bf16 (q | k | v column blocks, rows b*L + t),
@@ -105,6 +142,9 @@ def flexrel_attention(qkv: torch.Tensor, batch: int, heads: int, rel: torch.Tens
 
     Same contract as the reference ``flexrel_attention``
     (triton/src/fds_triton/kernels.py:422-442); ``kv_len`` is an addition.
+    ``balanced=False`` keeps one 256-row unit per CTA; ``grid_ctas > 0`` asks
+    for a split last wave of that many pieces whenever the shape allows it
+    (tests use it to cut units at small sizes).
     """
     _rows_operand(qkv, "qkv")
     rows, width = qkv.shape
@@ -143,6 +183,7 @@ def flexrel_attention(qkv: torch.Tensor, batch: int, heads: int, rel: torch.Tens
             kv_len=kv_ptr, status=_status(dev).data_ptr(),
             batch=batch, heads=heads, seq_len=length, head_dim=dim, dtype=_DTYPES[qkv.dtype],
             scale=1.0 / math.sqrt(dim), timeout_ns=int(timeout_ns), debug_flags=int(debug_flags),
+            **_schedule(dev, lib, balanced and kv_len is None, grid_ctas),
         )
         rc = lib.fds_flexrel_attn_fwd(ctypes.byref(args), _stream_ptr(dev))
     _raise_rc(rc, "fds_flexrel_attn_fwd")
@@ -202,13 +243,15 @@ def rope_split(qkv: torch.Tensor, length: int, heads: int, cos: torch.Tensor,
 
 def rope_attention(qkv: torch.Tensor, batch: int, heads: int, cos: torch.Tensor, sin: torch.Tensor,
                    out: torch.Tensor | None = None, scratch: torch.Tensor | None = None,
-                   *, timeout_ns: int = 0, debug_flags: int = 0) -> torch.Tensor:
+                   *, timeout_ns: int = 0, debug_flags: int = 0, balanced: bool = True,
+                   grid_ctas: int = 0) -> torch.Tensor:
     """DiT head self-attention: RoPE on q and k (frame index t = row % L), then
     bidirectional softmax(q k^T / 8) v. qkv [B*L, 3*HID] -> [B*L, HID].
 
     Replaces ``K.rope_split`` + ``F.scaled_dot_product_attention`` at
     triton/src/fds_triton/model.py:319-325. ``scratch`` ([B*L, 2*HID], qkv
     dtype) receives the rotated q | k; it is allocated when not given.
+    ``balanced`` / ``grid_ctas`` as in :func:`flexrel_attention`.
     """
     _rows_operand(qkv, "qkv")
     rows, width = qkv.shape
@@ -241,6 +284,7 @@ def rope_attention(qkv: torch.Tensor, batch: int, heads: int, cos: torch.Tensor,
             out_row_stride=out.stride(0) if rows > 1 else hid, status=_status(dev).data_ptr(),
             batch=batch, heads=heads, seq_len=length, head_dim=HEAD_DIM, dtype=_DTYPES[qkv.dtype],
             scale=1.0 / math.sqrt(HEAD_DIM), timeout_ns=int(timeout_ns), debug_flags=int(debug_flags),
+            **_schedule(dev, lib, balanced, grid_ctas),
         )
         rc = lib.fds_rope_attn_fwd(ctypes.byref(args), _stream_ptr(dev))
     _raise_rc(rc, "fds_rope_attn_fwd")

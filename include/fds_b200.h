@@ -10,6 +10,20 @@
  * Numerics: fp16 or bf16 operands, fp32 accumulation, fp32 online softmax in
  * log2 units, P rounded to the operand type for the P.V product (the same
  * rounding points as the reference's Triton kernels).
+ *
+ * Work is cut into units of 256 query rows of one (window, head), one per CTA.
+ * Workspace (optional, both attention entry points): with a workspace of at
+ * least fds_attn_workspace_bytes(grid_ctas) bytes, zero-filled once before its
+ * first use, the kernels may split the last wave: when whole units would leave
+ * part of it idle, the units of the last wave are cut into one piece per SM
+ * (grid_ctas = G pieces; 0 = one per SM), and the parts of a cut unit are
+ * merged through the workspace by whichever part finishes last (no CTA waits
+ * for another). Calls leave the workspace ready for the next call (no reset
+ * between calls or graph replays; zero it again after a call that reported a
+ * timeout); calls that may overlap on the GPU (different streams) need
+ * different workspaces. NULL keeps one unit per CTA. The split is used only
+ * without kv_len, and only where it shortens the launch (or always, when
+ * grid_ctas > 0 asks for it and the shape allows it); fds_attn_schedule tells.
  */
 #ifndef FDS_B200_H
 #define FDS_B200_H
@@ -20,7 +34,7 @@
 extern "C" {
 #endif
 
-#define FDS_ABI_VERSION 1
+#define FDS_ABI_VERSION 2
 
 #if defined(_WIN32)
 #define FDS_API __declspec(dllexport)
@@ -74,6 +88,9 @@ typedef struct FdsFlexRelArgs {
     float scale;              /* softmax scale on (qk + qr); the reference uses 1/sqrt(64) */
     int64_t timeout_ns;       /* bound on every in-kernel wait; <= 0 selects 2 s */
     int32_t debug_flags;      /* 0 in production */
+    void* workspace;          /* device, zero-filled once; or NULL (see "Workspace" above) */
+    int64_t workspace_bytes;
+    int32_t grid_ctas;        /* pieces of a split last wave; 0 = one per SM */
 } FdsFlexRelArgs;
 
 FDS_API int fds_flexrel_attn_fwd(const FdsFlexRelArgs* args, void* stream);
@@ -106,6 +123,9 @@ typedef struct FdsRopeArgs {
     float scale;              /* the reference uses 1/sqrt(64) (SDPA default) */
     int64_t timeout_ns;
     int32_t debug_flags;
+    void* workspace;          /* as in FdsFlexRelArgs */
+    int64_t workspace_bytes;
+    int32_t grid_ctas;
 } FdsRopeArgs;
 
 FDS_API int fds_rope_attn_fwd(const FdsRopeArgs* args, void* stream);
@@ -141,6 +161,18 @@ FDS_API const char* fds_last_error(void);
 
 /* Shared-memory bytes a CTA of the attention kernels requests (for diagnostics). */
 FDS_API int fds_attn_smem_bytes(void);
+
+/* Workspace bytes a split last wave of grid_ctas pieces needs (0 = one per SM
+ * of the current device; returns 0 and sets the error message if the device
+ * cannot be queried). */
+FDS_API int64_t fds_attn_workspace_bytes(int32_t grid_ctas);
+
+/* The launch layout the attention kernels would use (diagnostics, tests):
+ * out[0] = CTAs, out[1] = CTAs holding one whole unit each, out[2] = pieces of
+ * the split last wave (0: none). workspace_bytes = 0 means no workspace; the
+ * device is queried only when grid_ctas = 0 and a workspace is given. */
+FDS_API int fds_attn_schedule(int32_t batch, int32_t heads, int32_t seq_len, int32_t has_kv_len,
+                              int64_t workspace_bytes, int32_t grid_ctas, int64_t* out);
 
 #ifdef __cplusplus
 }
