@@ -49,9 +49,9 @@
 // Relative bias (encoder): bias(i, j) = q_i . rel[clamp(j - i, -64, 8) + 64].
 // Per query tile and item the MMA computes QR = Q . rel^T (N = 80, rows 73..79
 // zero) into the S columns; the softmax threads copy their row of QR (scaled
-// to log2 units) into shared memory as a padded table, T[m] = QR[clamp(m - 2 -
-// (row & 1), 0, 72)] for m in [0, 78), so that the bias of two adjacent keys is
-// one aligned 8-byte load at a clamped even index. A KV tile whose every (i, j) pair
+// to log2 units) into shared memory as a padded table, T[m] = QR[clamp(m - 4 -
+// (row & 3), 0, 72)] for m in [0, 84), so that the bias of four adjacent keys
+// is one aligned 16-byte load at a clamped index that is a multiple of 4. A KV tile whose every (i, j) pair
 // saturates the clamp adds a per-row constant (QR[i,0] on the left, QR[i,72]
 // on the right), which folds into the exponent's FFMA offset at no per-score
 // cost; only the (at most three) near-diagonal tiles gather the bias per
@@ -97,7 +97,7 @@ constexpr int kNumPos = 73;        // relative-key table rows
 constexpr int kClampLeft = 64;
 constexpr int kClampRight = 8;
 constexpr int kRelRows = 80;       // table rows padded to a multiple of 16 (MMA N)
-constexpr int kQrStride = 78;      // floats per row of the padded shared QR table (see RowSoftmax)
+constexpr int kQrStride = 84;      // floats per row of the padded shared QR table (see the header)
 constexpr int kMmaWarp0 = 0;       // MMA issuer of query tile 0 (tile 1: kMmaWarp0 + 2)
 constexpr int kLoadWarp = 1;
 constexpr int kTmemWarp = 3;
@@ -593,17 +593,19 @@ struct RowSoftmax {
         // score in log2 units = s * mult + cb
         float mult = sl;
         if constexpr (kBand) {
-            // keys n0 + c, n0 + c + 1 (c even) take QR[clamp(k)], QR[clamp(k + 1)]
-            // with k = n0 + c - i + 64: the padded table's entries m, m + 1 for
-            // m = clamp(k + 2 + (i & 1), 0, 76), which is even (k and i have the
-            // same parity: n0 and the tile's first row are multiples of 128)
-            const int e0 = n0 - i + kClampLeft + 2 + (i & 1);
+            // keys n0 + c .. n0 + c + 3 (c a multiple of 4) take QR[clamp(k)] ..
+            // QR[clamp(k + 3)] with k = n0 + c - i + 64: the padded table's entries
+            // m .. m + 3 for m = clamp(k + 4 + (i & 3), 0, 80), a multiple of 4
+            // (k + (i & 3) is: n0, c, 64 and the tile's first row are)
+            const int e0 = n0 - i + kClampLeft + 4 + (i & 3);
 #pragma unroll
-            for (int c = 0; c < 128; c += 2) {
-                const int m = min(max(e0 + c, 0), kQrStride - 2);
-                const float2 b = ld_shared_v2f32(qrow + 4u * m);
+            for (int c = 0; c < 128; c += 4) {
+                const int m = min(max(e0 + c, 0), kQrStride - 4);
+                const float4 b = ld_shared_v4f32(qrow + 4u * m);
                 s[c] = fmaf(s[c], sl, b.x);
                 s[c + 1] = fmaf(s[c + 1], sl, b.y);
+                s[c + 2] = fmaf(s[c + 2], sl, b.z);
+                s[c + 3] = fmaf(s[c + 3], sl, b.w);
             }
             mult = 1.f;
             cb = 0.f;
@@ -831,18 +833,19 @@ __device__ __forceinline__ void softmax_role(uint32_t sbase, uint32_t tmem, cons
             warp_arrive(rs.s_free, lane);  // the S columns may now receive the item's first S
             qr_left = __uint_as_float(a[0]) * sl;
             qr_right = __uint_as_float(d[kNumPos - 1 - 64]) * sl;
-            // padded table: QR[0] below, QR[72] above, the row at offset 2 + (i & 1)
-            const uint32_t t = qrow + 4u * (2 + (i & 1));
+            // padded table: QR[0] below, QR[72] above (written first), the row at
+            // offset 4 + (i & 3) over them
+            const uint32_t t = qrow + 4u * (4 + (i & 3));
 #pragma unroll
-            for (int m = 0; m < 3; ++m) st_shared_f32(qrow + 4u * m, qr_left);
+            for (int m = 0; m < 7; ++m) st_shared_f32(qrow + 4u * m, qr_left);
+#pragma unroll
+            for (int m = kQrStride - 8; m < kQrStride; ++m) st_shared_f32(qrow + 4u * m, qr_right);
 #pragma unroll
             for (int c = 0; c < 32; ++c) st_shared_f32(t + 4u * c, __uint_as_float(a[c]) * sl);
 #pragma unroll
             for (int c = 0; c < 32; ++c) st_shared_f32(t + 4u * (32 + c), __uint_as_float(c2[c]) * sl);
 #pragma unroll
             for (int c = 0; c < kNumPos - 64; ++c) st_shared_f32(t + 4u * (64 + c), __uint_as_float(d[c]) * sl);
-#pragma unroll
-            for (int m = kQrStride - 3; m < kQrStride; ++m) st_shared_f32(qrow + 4u * m, qr_right);
         }
 
         // Tiles in key order: [.., jb0) every pair left-saturated (bias QR[i,0]),

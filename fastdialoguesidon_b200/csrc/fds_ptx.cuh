@@ -75,9 +75,12 @@ __device__ __forceinline__ float ld_shared_f32(uint32_t addr) {
     asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
     return v;
 }
-__device__ __forceinline__ float2 ld_shared_v2f32(uint32_t addr) {
-    float2 v;
-    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+__device__ __forceinline__ float4 ld_shared_v4f32(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
     return v;
 }
 __device__ __forceinline__ void st_shared_f32(uint32_t addr, float v) {
