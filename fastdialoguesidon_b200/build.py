@@ -25,8 +25,8 @@ SOURCES = ["fds_capi.cu", "fds_rope_static.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 # The attention kernels split their register file with setmaxnreg
-# (csrc/attn_kernel.cuh RegSplit: 2 x 128 softmax threads at 224 or 216, 128
-# control threads at 56 or 72). That
+# (csrc/attn_kernel.cuh RegSplit: 2 x 128 softmax threads at 224 or 208, 128
+# control threads at 56 or 88). That
 # split assumes the CTA is launched with exactly this many registers per
 # thread; a different count could make the increase wait forever, so the build
 # refuses to produce a library in that case.

@@ -65,11 +65,12 @@
 //
 // Registers: launched at 168 per thread; the control warpgroup gives some back
 // and the two softmax warpgroups take the rest (RegSplit: 224 / 56 for the
-// encoder, 216 / 72 for the DiT; 256*224 + 128*56 = 256*216 + 128*72 =
+// encoder, 208 / 88 for the DiT; 256*224 + 128*56 = 256*208 + 128*88 =
 // 384*168), enough to hold a row of S (128 fp32) and of P (64 packed pairs) at
 // once while the MMA warps keep their item loop in registers (below 56 they
-// spill on the hand-off path). The splits are the measured best of 232 / 40,
-// 224 / 56 and 216 / 72 for each kernel.
+// spill on the hand-off path; the DiT's split P V hand-off needs more than 72).
+// The encoder's split is the measured best of 232 / 40, 224 / 56 and 216 / 72;
+// the DiT's is the largest softmax share at which neither role spills.
 //
 // Every wait is bounded by a globaltimer deadline; an expired wait records a
 // status bit, raises a CTA-wide abort flag, and every role then drains its
@@ -106,10 +107,18 @@ constexpr int kThreads = 384;
 constexpr int kLaunchRegs = 168;   // per thread at launch (checked at build time)
 template <bool kRelBias>
 struct RegSplit {
-    static constexpr int kSoftmax = kRelBias ? 224 : 216;
-    static constexpr int kControl = kRelBias ? 56 : 72;
+    static constexpr int kSoftmax = kRelBias ? 224 : 208;
+    static constexpr int kControl = kRelBias ? 56 : 88;
     static_assert(256 * kSoftmax + 128 * kControl <= kThreads * kLaunchRegs, "register split exceeds the launch pool");
     static_assert(kSoftmax % 8 == 0 && kControl % 8 == 0 && kControl >= 24, "setmaxnreg operand");
+};
+// P(j) handed to the MMA warp in two key halves (DiT): P(j) V(j) over keys
+// 0..63 starts while the softmax warps still exponentiate keys 64..127. The
+// encoder keeps one hand-off per tile: its near-diagonal gather leaves no
+// registers for a mid-tile one, and measured slower with it.
+template <bool kRelBias>
+struct PvSplit {
+    static constexpr bool kOn = !kRelBias;
 };
 constexpr int kTmemCols = 512;
 constexpr int kTmemS = 0;          // S_w at kTmemS + 128 w
@@ -147,7 +156,8 @@ struct Smem {
     static constexpr int kSFree = kSFull + 2;           // all 4 warps read S(j) out     [per query tile]
     static constexpr int kPFull = kSFree + 2;           // all 4 warps stored P(j)       [per query tile]
     static constexpr int kPvDone = kPFull + 2;          // P(j) V(j) complete            [per query tile]
-    static constexpr int kDrain = kPvDone + 2;          // per query tile: its MMA warp's drain
+    static constexpr int kPHalf = kPvDone + 2;          // all 4 warps stored P(j)'s keys 0..63 (split P V) [per query tile]
+    static constexpr int kDrain = kPHalf + 2;          // per query tile: its MMA warp's drain
     static constexpr int kNever = kDrain + 2;
     static constexpr int kNumBars = kNever + 1;
     // misc block: +0 TMEM base, +4 abort flag, +8 status word pointer,
@@ -440,16 +450,20 @@ struct TileMma {
         __syncwarp();
     }
 
-    // O_w (+)= P_w V(stage st)
+    // O_w (+)= P_w V(stage st) over keys [16 k0, 16 k1); the group that ends at
+    // key 128 completes the tile (P V done, V stage released)
+    template <int k0, int k1>
     __device__ __forceinline__ void pv(int st, bool accumulate) const {
         if (elect_one()) {
             const uint64_t dv = sw128_desc(sbase + Smem::v + st * kTileBytes);
 #pragma unroll
-            for (int k = 0; k < kBlockN / 16; ++k)
+            for (int k = k0; k < k1; ++k)
                 mma_ts(tmem + kTmemO + w * kHeadDim, tmem + kTmemP + w * (kBlockN / 2) + 8 * k, dv + 128 * k,
                        kIdescPV, (accumulate || k > 0) ? 1u : 0u);
-            mma_commit(bar(Smem::kPvDone + w));
-            mma_commit(bar(Smem::kVEmpty + st));
+            if (k1 == kBlockN / 16) {
+                mma_commit(bar(Smem::kPvDone + w));
+                mma_commit(bar(Smem::kVEmpty + st));
+            }
         }
         __syncwarp();
     }
@@ -527,12 +541,26 @@ __device__ __forceinline__ void mma_role(uint32_t sbase, uint32_t tmem, WaitCtl 
                 tc_fence_after();
                 mma.s(gn % kStages, j + 2 == nt);
             }
-            ok = warp_wait(mma.bar(Smem::kPFull + w), npv & 1, ctl, err);
-            ++npv;
-            if (ok) ok = warp_wait(mma.bar(Smem::kVFull + g % kStages), (g / kStages) & 1, ctl, err);
-            if (!ok) break;
-            tc_fence_after();
-            mma.pv(g % kStages, j > 0);
+            constexpr int kHalfSteps = kBlockN / 32;
+            if constexpr (PvSplit<kRelBias>::kOn) {
+                ok = warp_wait(mma.bar(Smem::kPHalf + w), npv & 1, ctl, err);
+                if (ok) ok = warp_wait(mma.bar(Smem::kVFull + g % kStages), (g / kStages) & 1, ctl, err);
+                if (!ok) break;
+                tc_fence_after();
+                mma.template pv<0, kHalfSteps>(g % kStages, j > 0);
+                ok = warp_wait(mma.bar(Smem::kPFull + w), npv & 1, ctl, err);
+                ++npv;
+                if (!ok) break;
+                tc_fence_after();
+                mma.template pv<kHalfSteps, 2 * kHalfSteps>(g % kStages, true);
+            } else {
+                ok = warp_wait(mma.bar(Smem::kPFull + w), npv & 1, ctl, err);
+                ++npv;
+                if (ok) ok = warp_wait(mma.bar(Smem::kVFull + g % kStages), (g / kStages) & 1, ctl, err);
+                if (!ok) break;
+                tc_fence_after();
+                mma.template pv<0, 2 * kHalfSteps>(g % kStages, j > 0);
+            }
         }
     }
     if (nw > 0) mma.drain(ctl);  // something was issued
@@ -564,7 +592,7 @@ struct RowSoftmax {
     uint32_t tS, tP, tO;
     float sl;
     uint32_t qrow;  // shared address of this row's Q.rel^T in log2 units (encoder)
-    uint32_t s_full, s_free, p_full, pv_done;  // barrier shared addresses
+    uint32_t s_full, s_free, p_half, p_full, pv_done;  // barrier shared addresses
     WaitCtl ctl;
     int i, kv_end, lane, t_begin;
     float m_run, l_run;
@@ -647,8 +675,27 @@ struct RowSoftmax {
 #pragma unroll
         for (int a = 0; a < 4; ++a) ls[a] = make_float2(0.f, 0.f);
         const float2 mult2 = make_float2(mult, mult), add2 = make_float2(add, add);
+        const bool later = j > t_begin;
+        constexpr bool kSplit = PvSplit<kRelBias>::kOn;
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
+            if (kSplit && c == 32) {
+                // keys 0..63 done: store them once P(j-1) V(j-1) is complete (it
+                // reads these P columns), after O is rescaled if the max moved
+                if (later) {
+                    ok = warp_wait(pv_done, pv_parity, ctl, err);
+                    pv_parity ^= 1;
+                    if (!ok) return false;
+                    tc_fence_after();
+                    if (__any_sync(0xffffffffu, rescale)) rescale_o_row(tO, alpha);
+                }
+                tmem_st32(tP + 0, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+            }
+            if (kSplit && c == 48) {
+                // the first half of P(j) V(j) may start (the store ran under 16 pairs)
+                tmem_wait_st();
+                warp_arrive(p_half, lane);
+            }
             float2 pp;
             if (c % 10 == 1 || c % 10 == 4 || c % 10 == 7) {
                 pp = exp2_poly2(s[2 * c], s[2 * c + 1], ky, kb);
@@ -663,18 +710,19 @@ struct RowSoftmax {
         ls[0] = fadd2(fadd2(ls[0], ls[1]), fadd2(ls[2], ls[3]));
         l_run = l_run * alpha + (ls[0].x + ls[0].y);
 
-        const bool later = j > t_begin;
-        if (later) {
-            // P(j-1) V(j-1) must be complete before its P columns are rewritten
-            // and before O is rescaled (its latency hides under the work above).
-            ok = warp_wait(pv_done, pv_parity, ctl, err);
-            pv_parity ^= 1;
-            if (!ok) return false;
-            tc_fence_after();
+        if constexpr (!kSplit) {
+            if (later) {
+                // P(j-1) V(j-1) must be complete before its P columns are rewritten
+                // and before O is rescaled (its latency hides under the work above).
+                ok = warp_wait(pv_done, pv_parity, ctl, err);
+                pv_parity ^= 1;
+                if (!ok) return false;
+                tc_fence_after();
+            }
+            tmem_st32(tP + 0, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
         }
-        tmem_st32(tP + 0, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
         tmem_st32(tP + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
-        if (later && __any_sync(0xffffffffu, rescale)) rescale_o_row(tO, alpha);
+        if (!kSplit && later && __any_sync(0xffffffffu, rescale)) rescale_o_row(tO, alpha);
         tmem_wait_st();
         warp_arrive(p_full, lane);
         return true;
@@ -792,6 +840,7 @@ __device__ __forceinline__ void softmax_role(uint32_t sbase, uint32_t tmem, cons
     rs.s_full = bars + 8u * (Smem::kSFull + wg);
     rs.s_free = bars + 8u * (Smem::kSFree + wg);
     rs.p_full = bars + 8u * (Smem::kPFull + wg);
+    rs.p_half = bars + 8u * (Smem::kPHalf + wg);
     rs.pv_done = bars + 8u * (Smem::kPvDone + wg);
     rs.ctl = ctl;
     rs.lane = lane;
@@ -998,6 +1047,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bars[Smem::kSFree + w], 4);   // one arrival per softmax warp
             mbar_init(&bars[Smem::kPFull + w], 4);
             mbar_init(&bars[Smem::kPvDone + w], 1);
+            mbar_init(&bars[Smem::kPHalf + w], 4);
         }
         for (int d = 0; d < 2; ++d) mbar_init(&bars[Smem::kDrain + d], 1);
         mbar_init(&bars[Smem::kNever], 1);
