@@ -1032,6 +1032,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // Launched after the previous kernel in the stream is allowed to finish:
+    // nothing below reads or writes global memory before grid_dependency_wait
+    // (the set-up, TMEM allocation and tensor-map prefetch overlap its tail).
+    grid_launch_dependents();
 
     if (threadIdx.x == 0) {
         mbar_init(&bars[Smem::kQ], 1);
@@ -1054,6 +1058,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         st_shared_volatile_u32(ctl.misc + 4, 0);  // abort flag
         st_shared_u64(ctl.misc + 8, reinterpret_cast<uint64_t>(p.status));
         st_shared_u64(ctl.misc + 16, static_cast<uint64_t>(p.timeout_ns > 0 ? p.timeout_ns : kDefaultTimeoutNs));
+        grid_dependency_wait();  // build_items reads kv_len
         st_shared_volatile_u32(ctl.misc + 28, static_cast<uint32_t>(build_items(p, sbase)));
         fence_barrier_init();
         fence_proxy_async_smem();
@@ -1071,6 +1076,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    grid_dependency_wait();
     const uint32_t tmem = *tmem_holder;
     const int n_items = static_cast<int>(ld_shared_volatile_u32(ctl.misc + 28));
 

@@ -6,9 +6,12 @@
 #include <cuda_runtime.h>
 
 #include <cstdarg>
+#include <cstdlib>
+#include <cstring>
 #include <cstdio>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "attn_kernel.cuh"
 #include "capi_internal.h"
@@ -111,6 +114,34 @@ int make_rel_map(CUtensorMap* map, const void* base, int dtype) {
     return FDS_OK;
 }
 
+// Kernels are launched with programmatic stream serialization: a launch may
+// start its CTAs while the previous kernel in the stream drains, and waits in
+// the kernel (griddepcontrol.wait) before touching memory. FDS_PDL=0 in the
+// environment turns this off (plain stream order).
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("FDS_PDL");
+        return v == nullptr || std::strcmp(v, "0") != 0;
+    }();
+    return on;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // SMs of the current device (cached per device); 0 if it cannot be queried.
 int sm_count() {
     static int cached[64];
@@ -205,8 +236,9 @@ int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
         p.counts = reinterpret_cast<uint32_t*>(base);
         p.parts = reinterpret_cast<float*>(base + kWsSlotsOffset);
     }
-    kern<<<static_cast<unsigned>(plan.grid), fds::kThreads, fds::Smem::alloc, stream>>>(mq, mk, mv, mr, p);
-    e = cudaGetLastError();
+    e = launch_pdl(kern, dim3(static_cast<unsigned>(plan.grid)), dim3(fds::kThreads), fds::Smem::alloc, stream, mq, mk,
+                   mv, mr, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
     return FDS_OK;
 }
@@ -333,15 +365,18 @@ static int launch_rope(const void* qkv, int64_t qkv_row_stride, const float* cos
     const int threads = 256;
     const int64_t blocks = (total + threads - 1) / threads;
     if (blocks > 0x7fffffffLL) return fail(FDS_ERR_INVALID_ARGUMENT, "rope: too many rows");
+    const dim3 grid(static_cast<unsigned>(blocks)), block(threads);
+    cudaError_t e;
     if (dtype == FDS_DTYPE_FP16)
-        fds::rope_rotate_kernel<__half><<<static_cast<unsigned>(blocks), threads, 0, s>>>(
-            static_cast<const __half*>(qkv), qkv_row_stride, cos_t, sin_t, static_cast<__half*>(dq),
-            static_cast<__half*>(dk), static_cast<__half*>(dv), dst_stride, rows, seq_len, heads);
+        e = launch_pdl(fds::rope_rotate_kernel<__half>, grid, block, 0, s, static_cast<const __half*>(qkv),
+                       qkv_row_stride, cos_t, sin_t, static_cast<__half*>(dq), static_cast<__half*>(dk),
+                       static_cast<__half*>(dv), dst_stride, rows, seq_len, heads);
     else
-        fds::rope_rotate_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), threads, 0, s>>>(
-            static_cast<const __nv_bfloat16*>(qkv), qkv_row_stride, cos_t, sin_t, static_cast<__nv_bfloat16*>(dq),
-            static_cast<__nv_bfloat16*>(dk), static_cast<__nv_bfloat16*>(dv), dst_stride, rows, seq_len, heads);
-    cudaError_t e = cudaGetLastError();
+        e = launch_pdl(fds::rope_rotate_kernel<__nv_bfloat16>, grid, block, 0, s,
+                       static_cast<const __nv_bfloat16*>(qkv), qkv_row_stride, cos_t, sin_t,
+                       static_cast<__nv_bfloat16*>(dq), static_cast<__nv_bfloat16*>(dk),
+                       static_cast<__nv_bfloat16*>(dv), dst_stride, rows, seq_len, heads);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "rope launch: %s", cudaGetErrorString(e));
     return FDS_OK;
 }

@@ -166,6 +166,13 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
     tma_load_2d(smem_u32(smem_dst), map, smem_u32(bar), x, y);
 }
 
+// Programmatic dependent launch: wait until the grid this one depends on has
+// completed and its memory is visible (returns at once without such a grid),
+// and let the next grid in the stream start its CTAs (they still wait here
+// before touching memory).
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

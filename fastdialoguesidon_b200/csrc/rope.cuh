@@ -35,6 +35,9 @@ __global__ void __launch_bounds__(256) rope_rotate_kernel(const T* __restrict__ 
                                                           const float* __restrict__ sin_t, T* __restrict__ dst_q,
                                                           T* __restrict__ dst_k, T* __restrict__ dst_v,
                                                           int64_t dst_stride, int rows, int seq_len, int heads) {
+    // programmatic dependent launch (see grid_dependency_wait)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int parts = dst_v != nullptr ? 3 : 2;
     const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t total = static_cast<int64_t>(rows) * heads * parts * 4;

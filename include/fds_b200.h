@@ -6,6 +6,10 @@
  * Every entry point launches on the given stream, never synchronises, never
  * allocates device memory, and returns FDS_OK or an error code before any
  * launch when an argument is invalid (fds_last_error() then holds a message).
+ * Kernels are launched with programmatic stream serialization: a launch may
+ * place its CTAs while the previous kernel in the stream drains, and they wait
+ * for that kernel to complete before touching memory, so stream order holds.
+ * FDS_PDL=0 in the environment launches in plain stream order instead.
  *
  * Numerics: fp16 or bf16 operands, fp32 accumulation, fp32 online softmax in
  * log2 units, P rounded to the operand type for the P.V product (the same
