@@ -11,7 +11,10 @@ under baseline/_ref (``fds_triton``; skipped when it is not installed):
   w2v-BERT encoder, run once with the reference's attention and once with this
   library's ``encoder_attention`` swapped in at the call the reference makes
   (model.py:290); both are compared with the fp32 HF forward of the same
-  weights.
+  weights. Likewise the reference's DiT stage (``TritonModel.dit``,
+  model.py:305-345) on a random-init 2-block CTM head, with ``rope_split`` +
+  SDPA (model.py:319-325) replaced by this library's ``rope_attention``,
+  against the fp32 ``CTMOneStep`` forward (reference/modeling.py:413-439).
 
 Tolerances: op level, max |difference| <= 2e-3 (both sides approximate the
 fp32 result within the fp16 bar); stage level, SNR of each fp16 pipeline
@@ -132,6 +135,70 @@ def test_encoder_stage_drop_in(cuda_device, ref):
     snr_theirs = O.snr_db(truth.cpu(), theirs.cpu())
     snr_ours = O.snr_db(truth.cpu(), ours.cpu())
     print(f"encoder stage vs fp32 HF: reference attention {snr_theirs:.2f} dB, this library {snr_ours:.2f} dB, "
+          f"pipelines apart {O.snr_db(theirs.cpu(), ours.cpu()):.2f} dB")
+    assert snr_theirs >= 30 and snr_ours >= 30, (snr_theirs, snr_ours)
+    assert abs(snr_ours - snr_theirs) <= 1.0, (snr_theirs, snr_ours)
+
+
+def _dit_stage(blocks=2, seed=0, max_seq=1000):
+    """A random-init CTM head (default PyTorch init) with its one-step wrapper
+    and speaker projections, and the reference's DiT stage prepared from them."""
+    from fds_triton import model as M
+    from fds_triton.reference import modeling as RM
+
+    torch.manual_seed(seed)
+    latent, enc_hidden = 64, 1024
+    head = RM.CTMTransformerHead(latent_size=latent, cond_size=2 * latent + enc_hidden, hidden_size=768,
+                                 num_layers=blocks, num_heads=12)
+    ctm = RM.CTMOneStep(head, dict(alpha_t=0.6, sigma_t=0.8, c_skip=0.25, c_out=0.75)).cuda().eval()
+    spk = [torch.nn.Linear(enc_hidden, latent).cuda().eval() for _ in range(2)]
+    bundle = types.SimpleNamespace(ctm=ctm, head=head,
+                                   encoder=types.SimpleNamespace(speaker_1=spk[0], speaker_2=spk[1]))
+    stage = object.__new__(M.TritonModel)  # DiT stage only
+    stage.gelu_tanh = True
+    stage.dtype = M.FP16
+    stage.device = torch.device("cuda")
+    with torch.no_grad():
+        stage._prep_dit(bundle, max_seq)
+    return M, stage, ctm, spk
+
+
+def test_dit_stage_drop_in(cuda_device, ref):
+    B, L = 1, 1000
+    M, stage, ctm, spk = _dit_stage(max_seq=L)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    hidden = torch.randn(B * L, 1024, generator=g, device="cuda")
+    noise = torch.randn(B, L, 64, generator=g, device="cuda")
+    stash = {}
+
+    def rope_split_stash(qkv, length, heads, cos, sin):  # keeps the call's inputs for the attention below
+        stash.update(qkv=qkv, length=length, heads=heads, cos=cos, sin=sin)
+        dummy = qkv.new_empty(qkv.shape[0], heads * 64)
+        return dummy, dummy, dummy
+
+    def attention_ours(q, k, v, *args, **kwargs):  # [B, H, L, 64], as the call site expects
+        qkv, length, heads = stash["qkv"], stash["length"], stash["heads"]
+        batch = qkv.shape[0] // length
+        out = F.rope_attention(qkv, batch, heads, stash["cos"], stash["sin"])
+        return out.view(batch, length, heads, 64).transpose(1, 2)
+
+    with torch.no_grad():
+        cond = torch.cat([spk[0](hidden), spk[1](hidden), hidden], dim=-1).view(B, L, -1)
+        truth = ctm(cond, noise).float().reshape(-1, 64)
+        h16 = hidden.half()
+        theirs = stage.dit(h16, noise).float().reshape(-1, 64)
+        saved_split, saved_sdpa = M.K.rope_split, Fn.scaled_dot_product_attention
+        M.K.rope_split = rope_split_stash
+        Fn.scaled_dot_product_attention = attention_ours
+        try:
+            ours = stage.dit(h16, noise).float().reshape(-1, 64)
+        finally:
+            M.K.rope_split, Fn.scaled_dot_product_attention = saved_split, saved_sdpa
+    F.check_status()
+    assert stash, "the stage did not reach the attention call"
+    snr_theirs = O.snr_db(truth.cpu(), theirs.cpu())
+    snr_ours = O.snr_db(truth.cpu(), ours.cpu())
+    print(f"DiT stage vs fp32 CTM head: reference attention {snr_theirs:.2f} dB, this library {snr_ours:.2f} dB, "
           f"pipelines apart {O.snr_db(theirs.cpu(), ours.cpu()):.2f} dB")
     assert snr_theirs >= 30 and snr_ours >= 30, (snr_theirs, snr_ours)
     assert abs(snr_ours - snr_theirs) <= 1.0, (snr_theirs, snr_ours)
