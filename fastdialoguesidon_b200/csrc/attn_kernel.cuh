@@ -568,6 +568,14 @@ __device__ __forceinline__ void mma_role(uint32_t sbase, uint32_t tmem, WaitCtl 
 
 // ---------------------------------------------------------------- softmax
 
+// Whether score pair c (of a tile's 64) is exponentiated by the FMA-pipe
+// polynomial instead of MUFU ex2: 3 pairs in 10 for the encoder, 2 in 10 for
+// the DiT (each the measured best of 10-35 % and of where in the 10 they sit).
+template <bool kRelBias>
+__device__ __forceinline__ constexpr bool poly_pair(int c) {
+    return kRelBias ? (c % 10 == 1 || c % 10 == 4 || c % 10 == 7) : (c % 10 == 2 || c % 10 == 7);
+}
+
 // O *= alpha for this thread's row (32 lanes of a warp, 64 columns). Rare (the
 // running max moves by more than the lazy threshold), so it is kept out of line:
 // its registers then never compete with the exponentials of the hot loop.
@@ -667,9 +675,9 @@ struct RowSoftmax {
         const float add = cb - m_run;
         const float ky = mult * (1.0f / kPolySpan), kb = (add - kPolyLo) * (1.0f / kPolySpan);
 
-        // exponentials into packed 16-bit pairs, held in registers; 3 of every
-        // 10 pairs go through the FMA-pipe polynomial so that the MUFU and FMA
-        // pipes carry similar loads
+        // exponentials into packed 16-bit pairs, held in registers; some pairs
+        // go through the FMA-pipe polynomial so that the MUFU and FMA pipes
+        // carry similar loads (poly_pair)
         uint32_t pk[64];
         float2 ls[4];
 #pragma unroll
@@ -697,7 +705,7 @@ struct RowSoftmax {
                 warp_arrive(p_half, lane);
             }
             float2 pp;
-            if (c % 10 == 1 || c % 10 == 4 || c % 10 == 7) {
+            if (poly_pair<kRelBias>(c)) {
                 pp = exp2_poly2(s[2 * c], s[2 * c + 1], ky, kb);
             } else {
                 const float2 x = ffma2(make_float2(s[2 * c], s[2 * c + 1]), mult2, add2);
