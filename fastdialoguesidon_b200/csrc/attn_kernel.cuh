@@ -699,8 +699,10 @@ struct RowSoftmax {
                 }
                 tmem_st32(tP + 0, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
             }
-            if (kSplit && c == 48) {
-                // the first half of P(j) V(j) may start (the store ran under 16 pairs)
+            if (kSplit && c == 40) {
+                // the first half of P(j) V(j) may start (the store ran under 8 pairs;
+                // measured best of pairs 34-56: earlier waits on the store, later
+                // delays the MMA)
                 tmem_wait_st();
                 warp_arrive(p_half, lane);
             }
