@@ -114,8 +114,9 @@ struct RegSplit {
 };
 // P(j) handed to the MMA warp in two key halves (DiT): P(j) V(j) over keys
 // 0..63 starts while the softmax warps still exponentiate keys 64..127. The
-// encoder keeps one hand-off per tile: its near-diagonal gather leaves no
-// registers for a mid-tile one, and measured slower with it.
+// encoder keeps one hand-off per tile: it measured slower with the split, on
+// its bias-free tiles too (its near-diagonal gather leaves no registers for a
+// mid-tile one).
 template <bool kRelBias>
 struct PvSplit {
     static constexpr bool kOn = !kRelBias;
