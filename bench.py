@@ -10,6 +10,19 @@ between steps). The QKV of layer i follows the stacking rule: x_{i+1} =
 x_i + Attn_i(x_i) W_out^T on an fp32 residual, x_0 ~ N(0,1), weights
 ~ N(0, 0.02), rel ~ N(0, 0.02) (random init, seeded per window).
 
+Beside the headline, the same line carries (all timed on the device with CUDA
+events, max over ranks):
+  dit         config 4: the 8-layer DiT RoPE attention of one window;
+  config3     config 3: a batch of 8 windows of random length (3.2-120 s),
+              bucketed to 10 s, key padding through kv_len; credited FLOPs
+              sum_b 13*4*16*64*L_b*kv_len_b (padding not credited);
+  throughput  config 5: 64 windows x (13-layer encoder + 8-layer DiT
+              attention), windows g, g+N, ... on rank g, windows/s =
+              64 / max-over-ranks time of one sweep;
+  e2e         the headline through the public API with host buffers, with the
+              measured host<->device copy bandwidth of the same pinned buffers
+              and the copy-bound time it implies.
+
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 Multi-GPU: launched under torch.distributed.run, one process per GPU; every
 rank owns whole windows (weak scaling, no data-path collective); the step time
@@ -62,6 +75,8 @@ def parse_args():
                          "unit: always one 256-row unit per CTA")
     ap.add_argument("--case", choices=("enc1", "dit1"), default=None,
                     help="profiling case: W + K eager launches of one layer (encoder or DiT) at L=6000")
+    ap.add_argument("--no-config3", action="store_true")
+    ap.add_argument("--no-throughput", action="store_true")
     return ap.parse_args()
 
 
@@ -156,21 +171,25 @@ class ClockSampler:
 
 
 def make_window(seed: int, device: torch.device, layers: int = ENC_LAYERS, length: int = L_WINDOW,
-                heads: int = ENC_HEADS):
-    """Per-layer fp16 QKV [L, 3*H*64] and rel [73, 64] for one window, stacked
-    on an fp32 residual through this library's attention (setup, untimed)."""
+                heads: int = ENC_HEADS, batch: int = 1, kv_len: torch.Tensor | None = None):
+    """Per-layer fp16 QKV [B*L, 3*H*64] and rel [73, 64] for one window (or a
+    padded batch of windows with key lengths kv_len), stacked on an fp32
+    residual through this library's attention (setup, untimed)."""
     import fastdialoguesidon_b200 as F
 
     hidden = heads * HEAD_DIM
     gen = torch.Generator(device=device).manual_seed(seed)
-    x = torch.randn(length, hidden, generator=gen, device=device)
+    x = torch.randn(batch * length, hidden, generator=gen, device=device)
+    if kv_len is not None:  # padded frames are zero, as the padded waveform's
+        pad = torch.arange(length, device=device)[None, :] >= kv_len.to(device)[:, None].long()
+        x[pad.reshape(-1)] = 0.0
     qkvs, rels = [], []
     for _ in range(layers):
         w_qkv = torch.randn(3 * hidden, hidden, generator=gen, device=device) * 0.02
         w_out = torch.randn(hidden, hidden, generator=gen, device=device) * 0.02
         rel = (torch.randn(73, HEAD_DIM, generator=gen, device=device) * 0.02).half()
         qkv = (x @ w_qkv.t()).half()
-        ctx = F.flexrel_attention(qkv, 1, heads, rel)
+        ctx = F.flexrel_attention(qkv, batch, heads, rel, kv_len=kv_len)
         x = x + ctx.float() @ w_out.t()
         qkvs.append(qkv)
         rels.append(rel)
@@ -178,16 +197,37 @@ def make_window(seed: int, device: torch.device, layers: int = ENC_LAYERS, lengt
     return qkvs, rels
 
 
-def time_graph(fn, steps: int, warmup: int, device: torch.device, dist_on: bool) -> float:
-    """Capture fn() once; W untimed replays; K timed replays between barrier +
-    synchronize on both sides; returns elapsed ms (CUDA events on the replay stream)."""
+def config3_lengths(seed: int = 3, batch: int = 8) -> tuple[list[int], list[int]]:
+    """Config 3: window lengths drawn uniformly from 3.2-120 s (frames =
+    ceil(50 s)), each rounded up to its 10 s bucket (a multiple of 500 frames);
+    returns (frames, buckets)."""
+    g = torch.Generator().manual_seed(seed)
+    secs = 3.2 + (120.0 - 3.2) * torch.rand(batch, generator=g, dtype=torch.float64)
+    frames = [min(L_WINDOW, int(math.ceil(float(t) * 50.0))) for t in secs]
+    buckets = [min(L_WINDOW, (f + 499) // 500 * 500) for f in frames]
+    return frames, buckets
+
+
+def make_dit_window(seed: int, device: torch.device):
+    """Per-layer fp16 DiT QKV [L, 3*12*64] (N(0, 0.55), the scale the DiT's
+    projections give) for one window."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    return [(torch.randn(L_WINDOW, 3 * DIT_HEADS * HEAD_DIM, generator=gen, device=device) * 0.55).half()
+            for _ in range(DIT_LAYERS)]
+
+
+def time_graph(fn, steps: int, warmup: int, device: torch.device, dist_on: bool, per_step: list | None = None) -> float:
+    """Capture fn() once (on the stream its eager warm-up ran on); W untimed
+    replays; K timed replays between barrier + synchronize on both sides;
+    returns elapsed ms (CUDA events on the replay stream). ``per_step``, if
+    given, receives each replay's own event time (for a median)."""
     s = torch.cuda.Stream(device)
     s.wait_stream(torch.cuda.current_stream(device))
     with torch.cuda.stream(s):
         fn()
     torch.cuda.current_stream(device).wait_stream(s)
     g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
+    with torch.cuda.graph(g, stream=s):
         fn()
     for _ in range(warmup):
         g.replay()
@@ -196,15 +236,17 @@ def time_graph(fn, steps: int, warmup: int, device: torch.device, dist_on: bool)
         torch.distributed.barrier()
     torch.cuda.synchronize(device)
     stream = torch.cuda.current_stream(device)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for _ in range(steps):
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    evs[0].record(stream)
+    for k in range(steps):
         g.replay()
-    end.record(stream)
+        evs[k + 1].record(stream)
     torch.cuda.synchronize(device)
     if dist_on:
         torch.distributed.barrier()
-    ms = start.elapsed_time(end)
+    ms = evs[0].elapsed_time(evs[-1])
+    if per_step is not None:
+        per_step.extend(evs[k].elapsed_time(evs[k + 1]) for k in range(steps))
     del g
     return ms
 
@@ -262,7 +304,37 @@ def e2e_encoder(qkvs, rels, steps: int, warmup: int, device: torch.device, dist_
     if dist_on:
         torch.distributed.barrier()
     F.check_status(device)
-    return start.elapsed_time(end), h2d, d2h
+    e2e_ms = start.elapsed_time(end)
+
+    # copy roofline: the same pinned buffers moved with no kernel in between,
+    # host->device alone, device->host alone, and both at once (full duplex),
+    # every rank at the same time as in the e2e run
+    def copies(h2d_on: bool, d2h_on: bool) -> float:
+        if dist_on:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(comp)
+        s_in.wait_stream(comp)
+        s_out.wait_stream(comp)
+        for _ in range(steps):
+            if h2d_on:
+                with torch.cuda.stream(s_in):
+                    for i in range(n):
+                        dev_in[i].copy_(host_in[i], non_blocking=True)
+                        dev_rel[i].copy_(host_rel[i], non_blocking=True)
+            if d2h_on:
+                with torch.cuda.stream(s_out):
+                    for i in range(n):
+                        host_out[i].copy_(dev_out[i], non_blocking=True)
+        comp.wait_stream(s_in)
+        comp.wait_stream(s_out)
+        b.record(comp)
+        torch.cuda.synchronize(device)
+        return a.elapsed_time(b) / steps
+
+    copy = {"h2d_ms": copies(True, False), "d2h_ms": copies(False, True), "both_ms": copies(True, True)}
+    return e2e_ms, h2d, d2h, copy
 
 
 _CPU_INPUTS = None
@@ -279,26 +351,47 @@ def _cpu_inputs():
     return _CPU_INPUTS
 
 
-def cpu_sample_ms_per_window(rows: int = 6000, threads: int | None = None) -> tuple[float, dict]:
-    """The oracle (fp32 torch, chunked like the reference's torch_core_chunked,
-    trt/src/fastdialoguesidon/flexrel_triton.py:298-329) on the host cores: the
-    first ``rows`` query rows of one layer of one window against all 6000 keys,
-    scaled to 13 layers x 6000 rows."""
-    from oracle import flexrel_oracle as O
+def reference_cpu_core():
+    """The reference's own fp32 CPU path, ``torch_core_chunked``
+    (trt/src/fastdialoguesidon/flexrel_triton.py:298-329), imported unmodified
+    from baseline/_ref when it is installed there; None otherwise."""
+    path = REPO / "baseline" / "_ref"
+    if not (path / "fastdialoguesidon" / "flexrel_triton.py").exists():
+        return None
+    if str(path) not in sys.path:
+        sys.path.insert(0, str(path))
+    try:
+        from fastdialoguesidon.flexrel_triton import torch_core_chunked
+    except Exception:  # noqa: BLE001 - fall back to the port, and say so
+        return None
+    return torch_core_chunked
 
+
+def cpu_layer_ms_per_window(threads: int | None = None) -> tuple[float, dict]:
+    """One full encoder layer of one window (6000 query rows x 16 heads x 6000
+    keys, fp32, 512-row chunks) on the host cores, scaled x13 layers to ms per
+    window. Runs the reference's own torch_core_chunked when baseline/_ref has
+    it ("reference"), else the oracle's restatement of it ("port")."""
     if threads:
         torch.set_num_threads(threads)
     q, k, v, rel = _cpu_inputs()
-    L = L_WINDOW
+    core = reference_cpu_core()
     t0 = time.perf_counter()
-    for start in range(0, rows, 512):
-        stop = min(start + 512, rows)
-        O.flexrel_rows(q, k, v, rel, start, stop)
+    if core is not None:
+        out = torch.empty_like(q)
+        core(q, k, v, rel, out, chunk=512)
+        kind, what = "reference", "reference torch_core_chunked (baseline/_ref, unmodified)"
+    else:
+        from oracle import flexrel_oracle as O
+
+        for start in range(0, L_WINDOW, 512):
+            O.flexrel_rows(q, k, v, rel, start, min(start + 512, L_WINDOW))
+        kind, what = "port", "oracle restatement of torch_core_chunked"
     dt = time.perf_counter() - t0
-    ms = dt * 1e3 * (L / rows) * ENC_LAYERS
-    return ms, {"cores": torch.get_num_threads(), "cpu_count": os.cpu_count(),
-                "sample": f"oracle fp32 core, {rows} query rows x 16 heads x 6000 keys of one layer "
-                          f"({dt:.2f} s), scaled x{L / rows:.2f} rows x 13 layers"}
+    return dt * 1e3 * ENC_LAYERS, {
+        "cores": torch.get_num_threads(), "cpu_count": os.cpu_count(), "kind": kind,
+        "sample": f"{what}, fp32: one full layer of the window (6000 query rows x 16 heads x 6000 keys, "
+                  f"{dt:.2f} s), x13 layers"}
 
 
 def reference_gpu_leg(qkvs, rels, outs, dit_inputs, device, steps: int = 5) -> dict:
@@ -366,19 +459,20 @@ def reference_gpu_leg(qkvs, rels, outs, dit_inputs, device, steps: int = 5) -> d
 
 
 def run_reference(args, rank: int) -> None:
-    """CPU arm: the oracle port of the reference's fp32 path on all host cores,
-    each step a 128-row sample of one layer scaled to a whole window."""
+    """CPU arm: the reference's fp32 path (its own torch_core_chunked from
+    baseline/_ref, else the oracle's port of it) on all host cores, each step
+    one full layer of the window, reported per window (x13 layers)."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    rows = 128
     for _ in range(max(args.warmup, 1)):
-        cpu_sample_ms_per_window(rows)
+        cpu_layer_ms_per_window()
     vals = []
     t0 = time.perf_counter()
+    info = {}
     for _ in range(args.steps):
-        ms, info = cpu_sample_ms_per_window(rows)
+        ms, info = cpu_layer_ms_per_window()
         vals.append(ms)
         if time.perf_counter() - t0 > 150:  # keep the arm within a few minutes
             break
@@ -388,11 +482,69 @@ def run_reference(args, rank: int) -> None:
         "n_gpus": args.gpus, "steps": len(vals), "warmup": args.warmup, "ms_per_step": round(value, 3),
         "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,0.64) q/k/v, N(0,0.02) rel)", "config": config_dict(args.gpus),
-        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": info["kind"],
                          "sample": info["sample"] + "; median over steps"},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def config3_leg(args, rank: int, device: torch.device, dist_on: bool, bal: bool) -> dict:
+    """Config 3: a batch of 8 windows of seeded random length, bucketed to 10 s,
+    padded to the longest bucket, keys masked past each window's true length
+    (kv_len); 13 layers per step in one graph. Every rank runs its own batch."""
+    import fastdialoguesidon_b200 as F
+
+    frames, buckets = config3_lengths()
+    B, Lmax = len(frames), max(buckets)
+    kv = torch.tensor(frames, dtype=torch.int32, device=device)
+    qkvs, rels = make_window(seed=3000 + rank, device=device, length=Lmax, batch=B, kv_len=kv)
+    outs = [torch.empty(B * Lmax, ENC_HEADS * HEAD_DIM, dtype=torch.float16, device=device) for _ in qkvs]
+
+    def step():
+        for q, r, o in zip(qkvs, rels, outs):
+            F.flexrel_attention(q, B, ENC_HEADS, r, out=o, kv_len=kv)
+
+    steps = max(3, args.steps // 4)
+    per = []
+    ms = time_graph(step, steps, max(3, min(args.warmup, 5)), device, dist_on, per_step=per)
+    F.check_status(device)
+    credited = sum(ENC_LAYERS * 4 * ENC_HEADS * HEAD_DIM * lb * kb for lb, kb in zip(buckets, frames))
+    computed = sum(ENC_LAYERS * 4 * ENC_HEADS * HEAD_DIM * Lmax * ((kb + 127) // 128 * 128) for kb in frames)
+    del qkvs, outs
+    return {"ms": ms, "steps": steps, "median": statistics.median(per), "credited": credited,
+            "computed": computed, "frames": frames, "buckets": buckets, "Lmax": Lmax}
+
+
+def throughput_leg(args, rank: int, world: int, device: torch.device, dist_on: bool, bal: bool) -> dict:
+    """Config 5: 64 windows x (13-layer encoder + 8-layer DiT attention); rank g
+    takes windows g, g+N, ...; one sweep over this rank's windows is captured
+    in one CUDA graph."""
+    import fastdialoguesidon_b200 as F
+
+    mine = list(range(rank, 64, world))
+    enc = [make_window(seed=5000 + w, device=device) for w in mine]
+    dit = [make_dit_window(seed=6000 + w, device=device) for w in mine]
+    cos, sin = F.rope_tables(L_WINDOW, device)
+    eout = torch.empty(L_WINDOW, ENC_HEADS * HEAD_DIM, dtype=torch.float16, device=device)
+    dout = torch.empty(L_WINDOW, DIT_HEADS * HEAD_DIM, dtype=torch.float16, device=device)
+    scratch = torch.empty(L_WINDOW, 2 * DIT_HEADS * HEAD_DIM, dtype=torch.float16, device=device)
+
+    def sweep():
+        for (qkvs, rels), dq in zip(enc, dit):
+            for q, r in zip(qkvs, rels):
+                F.flexrel_attention(q, 1, ENC_HEADS, r, out=eout, balanced=bal)
+            for q in dq:
+                F.rope_attention(q, 1, DIT_HEADS, cos, sin, out=dout, scratch=scratch, balanced=bal)
+
+    steps = max(2, min(args.steps, 5))
+    per = []
+    with ClockSampler(device) as clocks:
+        ms = time_graph(sweep, steps, 2, device, dist_on, per_step=per)
+    F.check_status(device)
+    del enc, dit
+    return {"ms": ms, "steps": steps, "median": statistics.median(per), "windows_here": len(mine),
+            "clocks": clocks.summary()}
 
 
 def run_ours(args, rank: int, world: int, local_rank: int) -> None:
@@ -412,20 +564,19 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         for q, r, o in zip(qkvs, rels, outs):
             F.flexrel_attention(q, 1, ENC_HEADS, r, out=o, balanced=bal)
 
+    per_step: list[float] = []
     with ClockSampler(device) as clocks:
-        ms = time_graph(enc_step, args.steps, args.warmup, device, dist_on)
+        ms = time_graph(enc_step, args.steps, args.warmup, device, dist_on, per_step=per_step)
     F.check_status(device)
+    med = statistics.median(per_step)
     e2e_steps = max(3, min(args.steps, 60))
-    e2e_ms, h2d, d2h = e2e_encoder(qkvs, rels, e2e_steps, max(3, min(args.warmup, 5)), device, dist_on, bal)
+    e2e_ms, h2d, d2h, copy = e2e_encoder(qkvs, rels, e2e_steps, max(3, min(args.warmup, 5)), device, dist_on,
+                                         bal)
 
     dit = None
     dit_inputs = None
     if not args.no_dit:
-        dq = []
-        gen = torch.Generator(device=device).manual_seed(2000 + rank)
-        for _ in range(DIT_LAYERS):
-            dq.append((torch.randn(L_WINDOW, 3 * DIT_HEADS * HEAD_DIM, generator=gen, device=device)
-                       * 0.55).half())
+        dq = make_dit_window(seed=2000 + rank, device=device)
         cos, sin = F.rope_tables(L_WINDOW, device)
         dout = [torch.empty(L_WINDOW, DIT_HEADS * HEAD_DIM, dtype=torch.float16, device=device) for _ in dq]
         scratch = torch.empty(L_WINDOW, 2 * DIT_HEADS * HEAD_DIM, dtype=torch.float16, device=device)
@@ -435,15 +586,21 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                 F.rope_attention(q, 1, DIT_HEADS, cos, sin, out=o, scratch=scratch, balanced=bal)
 
         dsteps = max(3, args.steps // 2)
-        dms = time_graph(dit_step, dsteps, args.warmup, device, dist_on)
+        dper: list[float] = []
+        dms = time_graph(dit_step, dsteps, args.warmup, device, dist_on, per_step=dper)
         F.check_status(device)
-        dit = (dms, dsteps)
+        dit = (dms, dsteps, statistics.median(dper))
         dit_inputs = (dq, cos, sin, dout)
 
-    t = torch.tensor([ms, e2e_ms, dit[0] if dit else 0.0], dtype=torch.float64, device=device)
+    c3 = None if args.no_config3 else config3_leg(args, rank, device, dist_on, bal)
+    tp = None if args.no_throughput else throughput_leg(args, rank, world, device, dist_on, bal)
+
+    vals = [ms, e2e_ms, copy["h2d_ms"], copy["d2h_ms"], copy["both_ms"], dit[0] if dit else 0.0,
+            c3["ms"] if c3 else 0.0, tp["ms"] if tp else 0.0]
+    t = torch.tensor(vals, dtype=torch.float64, device=device)
     if dist_on:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms, e2e_ms, dms = (float(x) for x in t.tolist())
+    ms, e2e_ms, h2d_ms, d2h_ms, both_ms, dms, c3_ms, tp_ms = (float(x) for x in t.tolist())
 
     if rank == 0:
         K = args.steps
@@ -453,12 +610,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         achieved = FLOP_ENC_LAYER / (per_launch_ms * 1e-3) / 1e12
         peak, peak_note = measured_peak()
         traffic = ncu_traffic()
+        e2e_value = e2e_ms / (e2e_steps * world)
         line = {
             "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": round(ms / K, 4), "higher_is_better": False,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic (seeded random-init weights / inputs of the config-2 shapes)",
             "config": config_dict(world),
+            "median_ms_per_step": round(med, 4),
             "tflops": round(FLOP_ENC_LAYER * ENC_LAYERS * windows / (ms * 1e-3) / 1e12, 1),
             "pct_dense_fp16_peak": round(100 * achieved / DATASHEET_DENSE_FP16_TFLOPS, 1),
             "windows_per_s": round(windows / (ms * 1e-3), 2),
@@ -466,23 +625,56 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "kernel": "fds::attn_fwd_kernel<__half, true> (one encoder layer, 147.456 GFLOP)",
                          "peak_note": peak_note},
-            "e2e": {"value": round(e2e_ms / (e2e_steps * world), 4), "unit": UNIT,
+            "e2e": {"value": round(e2e_value, 4), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "note": "public API flexrel_attention, pinned host QKV/rel in, context out, per step"},
+                    "note": "public API flexrel_attention, pinned host QKV/rel in, context out, per step",
+                    "copy_roofline": {
+                        "h2d_gbs_per_gpu": round(h2d / (h2d_ms * 1e-3) / 1e9, 1),
+                        "d2h_gbs_per_gpu": round(d2h / (d2h_ms * 1e-3) / 1e9, 1),
+                        "both_ms_per_step": round(both_ms, 4),
+                        "bound_ms_per_window": round(both_ms / world, 4),
+                        "frac": round((both_ms / world) / e2e_value, 3),
+                        "note": "the same pinned buffers copied with no kernel (h2d alone, d2h alone, both at "
+                                "once on every rank); e2e is copy-bound when frac is near 1"}},
             "gpu_launches": K * ENC_LAYERS,
             "clocks": clocks.summary(),
         }
         if dit:
             dsteps = dit[1]
-            dper = dms / (dsteps * DIT_LAYERS)
+            dper_ms = dms / (dsteps * DIT_LAYERS)
             line["dit"] = {"workload": "config4: 8-layer DiT RoPE attention, L=6000, 12 x 64 heads",
-                           "ms_per_window": round(dms / dsteps, 4),
-                           "tflops": round(FLOP_DIT_LAYER / (dper * 1e-3) / 1e12, 1),
+                           "ms_per_window": round(dms / dsteps, 4), "median_ms_per_window": round(dit[2], 4),
+                           "tflops": round(FLOP_DIT_LAYER / (dper_ms * 1e-3) / 1e12, 1),
+                           "frac": round(FLOP_DIT_LAYER / (dper_ms * 1e-3) / 1e12 / peak, 4),
                            "steps": dsteps, "launches_per_window": 2 * DIT_LAYERS}
+        if c3:
+            per_batch = c3_ms / c3["steps"]
+            line["config3"] = {
+                "workload": "config3: batch of 8 windows, lengths U(3.2, 120) s (seed 3), 10 s buckets, "
+                            "padded to the longest bucket, kv_len key padding, 13 layers",
+                "frames": c3["frames"], "buckets": c3["buckets"], "padded_len": c3["Lmax"],
+                "ms_per_batch": round(per_batch, 4), "median_ms_per_batch": round(c3["median"], 4),
+                "batches_per_s": round(world / (per_batch * 1e-3), 2),
+                "credited_tflops": round(c3["credited"] * world / (per_batch * 1e-3) / 1e12, 1),
+                "credited_rule": "sum_b 13*4*16*64*L_b*kv_len_b (L_b the window's own bucket)",
+                "computed_tflops": round(c3["computed"] * world / (per_batch * 1e-3) / 1e12, 1),
+                "steps": c3["steps"]}
+        if tp:
+            sweep_ms = tp_ms / tp["steps"]
+            line["throughput"] = {
+                "workload": "config5: 64 windows x (13-layer encoder rel-bias attention + 8-layer DiT RoPE "
+                            "attention), L=6000, windows g, g+N, ... on rank g, no collectives",
+                "windows": 64, "windows_per_gpu": tp["windows_here"], "n_gpus": world,
+                "ms_per_sweep": round(sweep_ms, 3), "median_ms_per_sweep_rank0": round(tp["median"], 3),
+                "windows_per_s": round(64 / (sweep_ms * 1e-3), 2),
+                "tflops": round(64 * (ENC_LAYERS * FLOP_ENC_LAYER + DIT_LAYERS * FLOP_DIT_LAYER)
+                                / (sweep_ms * 1e-3) / 1e12, 1),
+                "steps": tp["steps"], "clocks_rank0": tp["clocks"],
+                "timing": "one CUDA graph per rank per sweep; max over ranks of the device time"}
         if world == 1 and not args.no_cpu_baseline:
-            cms, info = cpu_sample_ms_per_window(rows=1024, threads=os.cpu_count())
+            cms, info = cpu_layer_ms_per_window(threads=os.cpu_count())
             line["cpu_baseline"] = {"value": round(cms, 1), "unit": UNIT, "cores": info["cores"],
-                                    "kind": "port", "sample": info["sample"]}
+                                    "kind": info["kind"], "sample": info["sample"]}
         if world == 1 and not args.no_reference_gpu:
             line["reference_gpu"] = reference_gpu_leg(qkvs, rels, outs, dit_inputs, device)
         print(json.dumps(line), flush=True)

@@ -30,7 +30,7 @@ FDS_DEBUG_FORCE_TIMEOUT = 0x1
 
 FDS_ROPE_STATIC_SCRATCH_BYTES = 20 * 1024 * 1024
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 # every symbol include/fds_b200.h declares (checked by the CPU test suite)
 EXPORTED_SYMBOLS = (
@@ -66,6 +66,7 @@ class FdsFlexRelArgs(ctypes.Structure):
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_int64),
         ("grid_ctas", ctypes.c_int32),
+        ("status_host", ctypes.c_void_p),
     ]
 
 
@@ -90,6 +91,7 @@ class FdsRopeArgs(ctypes.Structure):
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_int64),
         ("grid_ctas", ctypes.c_int32),
+        ("status_host", ctypes.c_void_p),
     ]
 
 

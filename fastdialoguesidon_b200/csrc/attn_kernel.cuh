@@ -162,9 +162,9 @@ struct Smem {
     static constexpr int kNever = kDrain + 2;
     static constexpr int kNumBars = kNever + 1;
     // misc block: +0 TMEM base, +4 abort flag, +8 status word pointer,
-    // +16 wait timeout (ns), +28 item count
+    // +16 wait timeout (ns), +28 item count, +32 host status mirror pointer
     static constexpr int misc = bars + kNumBars * 8;
-    static constexpr int items = (misc + 32 + 15) / 16 * 16;  // kMaxItems x 2 int4
+    static constexpr int items = (misc + 40 + 15) / 16 * 16;  // kMaxItems x 2 int4
     static constexpr int total = items + kMaxItems * 32;
     static constexpr int alloc = total + 1024;  // slack for 1024-byte alignment
 };
@@ -177,6 +177,7 @@ struct AttnParams {
     int64_t out_stride;       // elements
     const int32_t* kv_len;    // [batch] or null (always null when the last wave is split)
     int32_t* status;          // or null
+    int32_t* status_host;     // mapped pinned host mirror of the status bits, or null
     int64_t timeout_ns;
     int32_t heads;
     int32_t seq_len;
@@ -360,6 +361,13 @@ __device__ __forceinline__ void raise_abort(WaitCtl ctl, int err_bit) {
     st_shared_volatile_u32(ctl.misc + 4, 1);
     int* status = reinterpret_cast<int*>(ld_shared_u64(ctl.misc + 8));
     if (status) atomicOr(status, err_bit);
+    // host-visible mirror: a plain read-modify-write of mapped host memory
+    // (only on this error path), which the host can poll without a sync
+    volatile int* mirror = reinterpret_cast<volatile int*>(ld_shared_u64(ctl.misc + 32));
+    if (mirror) {
+        *mirror = *mirror | err_bit;
+        __threadfence_system();
+    }
 }
 
 // Wait for completion of phase `parity` of the mbarrier at shared address
@@ -1068,6 +1076,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(&bars[Smem::kNever], 1);
         st_shared_volatile_u32(ctl.misc + 4, 0);  // abort flag
         st_shared_u64(ctl.misc + 8, reinterpret_cast<uint64_t>(p.status));
+        st_shared_u64(ctl.misc + 32, reinterpret_cast<uint64_t>(p.status_host));
         st_shared_u64(ctl.misc + 16, static_cast<uint64_t>(p.timeout_ns > 0 ? p.timeout_ns : kDefaultTimeoutNs));
         grid_dependency_wait();  // build_items reads kv_len
         st_shared_volatile_u32(ctl.misc + 28, static_cast<uint32_t>(build_items(p, sbase)));

@@ -5,6 +5,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdlib>
 #include <cstring>
@@ -54,20 +55,24 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// Device must be compute capability 10.0 (B200 / sm_100a). Cached per device.
+// Device must be compute capability 10.0 (B200 / sm_100a). Cached per device;
+// the entries are atomics so that first calls from several host threads do not
+// race (every thread computes the same value).
 int check_device() {
-    static int cached[64];  // 0 unknown, 1 ok, 2 unsupported
+    static std::atomic<int> cached[64];  // 0 unknown, 1 ok, 2 unsupported
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
     if (dev < 0 || dev >= 64) return fail(FDS_ERR_UNSUPPORTED_DEVICE, "device index %d out of range", dev);
-    if (cached[dev] == 0) {
+    int state = cached[dev].load(std::memory_order_relaxed);
+    if (state == 0) {
         int major = 0, minor = 0;
         cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
         cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
-        cached[dev] = (major == 10 && minor == 0) ? 1 : 2;
+        state = (major == 10 && minor == 0) ? 1 : 2;
+        cached[dev].store(state, std::memory_order_relaxed);
     }
-    if (cached[dev] != 1)
+    if (state != 1)
         return fail(FDS_ERR_UNSUPPORTED_DEVICE, "device %d is not sm_100 (B200); this library is built for sm_100a",
                     dev);
     return FDS_OK;
@@ -142,17 +147,18 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
-// SMs of the current device (cached per device); 0 if it cannot be queried.
+// SMs of the current device (cached per device, atomically as above); 0 if it
+// cannot be queried.
 int sm_count() {
-    static int cached[64];
+    static std::atomic<int> cached[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
-    if (cached[dev] == 0) {
-        int n = 0;
+    int n = cached[dev].load(std::memory_order_relaxed);
+    if (n == 0) {
         if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
-        cached[dev] = n;
+        cached[dev].store(n, std::memory_order_relaxed);
     }
-    return cached[dev];
+    return n;
 }
 
 // Workspace of the split last wave for up to G pieces: the part counts (one
@@ -342,6 +348,7 @@ int fds_flexrel_attn_fwd(const FdsFlexRelArgs* a, void* stream) {
     p.out_stride = a->out_row_stride;
     p.kv_len = a->kv_len;
     p.status = a->status;
+    p.status_host = a->status_host;
     p.timeout_ns = a->timeout_ns;
     p.heads = a->heads;
     p.seq_len = a->seq_len;
@@ -414,6 +421,7 @@ int fds_rope_attn_fwd(const FdsRopeArgs* a, void* stream) {
     p.out_stride = a->out_row_stride;
     p.kv_len = nullptr;
     p.status = a->status;
+    p.status_host = a->status_host;
     p.timeout_ns = a->timeout_ns;
     p.heads = a->heads;
     p.seq_len = a->seq_len;

@@ -20,7 +20,10 @@
 //     fds_rope_attn_fwd_static call made on it).
 //   * The first call on a device looks up the array's device address
 //     (cudaGetSymbolAddress, with that device current) and caches it; make
-//     that first call before any stream capture.
+//     that first call before any stream capture. The cached address does not
+//     survive cudaDeviceReset (the device's module is unloaded with the
+//     context); do not call this entry point again on a device after a reset.
+//   * The stream must belong to the current device (checked).
 //   * All calls share the one array and it keeps the previous call's contents:
 //     calls whose kernels overlap on the GPU (different streams, or different
 //     graphs replayed concurrently) race on it. Nothing in it needs clearing:
@@ -63,6 +66,18 @@ extern "C" FDS_API int fds_rope_attn_fwd_static(const FdsRopeArgs* args, void* s
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return set_error(FDS_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
     if (dev < 0 || dev >= 64) return set_error(FDS_ERR_UNSUPPORTED_DEVICE, "device index %d out of range", dev);
+    // the array's address belongs to the current device: a stream of another
+    // device would run the kernels against that device's memory
+    if (stream != nullptr) {
+        int stream_dev = -1;
+        e = cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &stream_dev);
+        if (e != cudaSuccess) return set_error(FDS_ERR_CUDA, "cudaStreamGetDevice: %s", cudaGetErrorString(e));
+        if (stream_dev != dev)
+            return set_error(FDS_ERR_INVALID_ARGUMENT,
+                             "the stream belongs to device %d but device %d is current; make the stream's device "
+                             "current before calling fds_rope_attn_fwd_static",
+                             stream_dev, dev);
+    }
     void* ptr = nullptr;
     {
         std::lock_guard<std::mutex> guard(g_lock);

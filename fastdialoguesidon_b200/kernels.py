@@ -8,19 +8,30 @@ dispatch), no autotuning, no host synchronisation and no allocation other than
 ``out`` (and the DiT's rotated-q|k scratch), so every call is safe inside
 ``torch.cuda.graph`` capture once the device has run one eager call.
 
-Schedule: each (device, stream) gets one zero-filled workspace (about 20 MB on
-a 148-SM B200, created on its first call there) that lets the library split
-the last wave -- when whole 256-row units would leave part of it idle, its
-units are cut into one piece per SM and the parts merged through the
-workspace. Calls on one stream are ordered, so they share it safely; a
-workspace created during graph capture belongs to the graph's memory pool and
-is zero-filled by a node of that graph. After a reported timeout
-(:func:`check_status`) the device's workspaces are zero-filled again.
+Schedule: each (device, stream) gets one zero-filled workspace (about 31 MB on
+a 148-SM B200) that lets the library split the last wave -- when whole
+256-row units would leave part of it idle, its units are cut into one piece
+per SM and the parts merged through the workspace. Calls on one stream are
+ordered, so they share it safely. Workspaces are never allocated inside a CUDA
+graph capture: the first eager call on a device also zero-fills two spare
+workspaces (and waits for that fill once), and a capture on a stream that has
+none takes a spare; with no spare left the captured call keeps one unit per
+CTA. After a reported timeout (:func:`check_status`) the device's workspaces
+are zero-filled again.
 
 Errors: invalid arguments raise :class:`FdsError` before any launch. It
 subclasses both ``AssertionError`` (what the reference's ``assert`` checks
 raise, ``kernels.py:430, 641``) and ``RuntimeError``. A missing native library
 or a non-CUDA tensor raises as well: there is no CPU fallback.
+
+Bounded-wait timeouts: a kernel whose wait expires records status bits in a
+device word and in a pinned host mirror of it. Every op call first reads the
+mirror (host memory, no synchronisation) and raises :class:`FdsError` if a
+previous call on that device timed out, so a drop-in caller that never calls
+:func:`check_status` still sees the failure at its next call (at the latest
+its next window). :func:`check_status` synchronises, reports and clears both
+words and re-zeroes the workspaces; a caller that wants the error attributed
+to its window calls it once per window.
 """
 
 from __future__ import annotations
@@ -45,7 +56,10 @@ class FdsError(AssertionError, RuntimeError):
 
 _DTYPES = {torch.float16: N.FDS_DTYPE_FP16, torch.bfloat16: N.FDS_DTYPE_BF16}
 _status_words: dict[int, torch.Tensor] = {}
+_status_mirrors: dict[int, torch.Tensor] = {}
 _workspaces: dict[tuple[int, int], torch.Tensor] = {}
+_spare_workspaces: dict[int, list[torch.Tensor]] = {}
+_SPARE_WORKSPACES = 2
 
 
 def _check(cond: bool, msg: str) -> None:
@@ -53,14 +67,40 @@ def _check(cond: bool, msg: str) -> None:
         raise FdsError(msg)
 
 
+def _dev_index(device: torch.device) -> int:
+    return device.index if device.index is not None else torch.cuda.current_device()
+
+
 def _status(device: torch.device) -> torch.Tensor:
     """Per-device int32 word the kernels OR their bounded-wait error bits into."""
-    idx = device.index if device.index is not None else torch.cuda.current_device()
+    idx = _dev_index(device)
     st = _status_words.get(idx)
     if st is None:
         st = torch.zeros(4, dtype=torch.int32, device=torch.device("cuda", idx))
         _status_words[idx] = st
     return st
+
+
+def _status_mirror(device: torch.device) -> torch.Tensor:
+    """Per-device pinned (mapped) host word the kernels mirror their error bits
+    into; read by the host without synchronising."""
+    idx = _dev_index(device)
+    m = _status_mirrors.get(idx)
+    if m is None:
+        m = torch.zeros(4, dtype=torch.int32).pin_memory()
+        _status_mirrors[idx] = m
+    return m
+
+
+def _raise_if_timed_out(device: torch.device) -> None:
+    """Raise (without a device sync) if a kernel on ``device`` reported a
+    timeout that :func:`check_status` has not cleared yet."""
+    m = _status_mirrors.get(_dev_index(device))
+    if m is not None:
+        bits = int(m[0])
+        if bits:
+            raise FdsError(f"an earlier FDS kernel on cuda:{_dev_index(device)} reported a bounded-wait "
+                           f"timeout (status bits 0x{bits:x}); call check_status() to clear it")
 
 
 def check_status(device: torch.device | int | None = None, clear: bool = True) -> int:
@@ -69,13 +109,18 @@ def check_status(device: torch.device | int | None = None, clear: bool = True) -
     dev = torch.device("cuda", torch.cuda.current_device() if device is None else
                        (device if isinstance(device, int) else device.index))
     st = _status(dev)
+    mirror = _status_mirror(dev)
     torch.cuda.synchronize(dev)
-    bits = int(st[0].item())
+    bits = int(st[0].item()) | int(mirror[0])
     if clear and bits:
         st.zero_()
+        mirror.zero_()
         for (idx, _), ws in _workspaces.items():
             if idx == dev.index:
                 ws.zero_()  # an aborted split may leave part counts behind
+        for ws in _spare_workspaces.get(dev.index, []):
+            ws.zero_()
+        torch.cuda.synchronize(dev)
     if bits:
         raise FdsError(f"FDS kernel on {dev} reported a bounded-wait timeout (status bits 0x{bits:x})")
     return bits
@@ -85,27 +130,43 @@ def _stream_ptr(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
-def _workspace(device: torch.device, lib) -> tuple[int, int]:
-    """(pointer, bytes) of the balanced-schedule workspace of ``device``'s
-    current stream; the C library leaves it ready for the next call."""
-    idx = device.index if device.index is not None else torch.cuda.current_device()
+def _workspace(device: torch.device, lib) -> torch.Tensor | None:
+    """The balanced-schedule workspace of ``device``'s current stream (the C
+    library leaves it ready for the next call), or None inside a graph capture
+    that finds neither one nor a spare (never allocated during capture: the
+    graph pool would zero it only at replay)."""
+    idx = _dev_index(device)
     key = (idx, _stream_ptr(device))
     ws = _workspaces.get(key)
-    if ws is None:
+    if ws is not None:
+        return ws
+    if torch.cuda.is_current_stream_capturing():
+        spares = _spare_workspaces.get(idx)
+        if not spares:
+            return None
+        ws = spares.pop()
+    else:
         nbytes = int(lib.fds_attn_workspace_bytes(0))
         if nbytes <= 0:
             raise FdsError(f"fds_attn_workspace_bytes failed: {N.last_error()}")
-        ws = torch.zeros(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
-        _workspaces[key] = ws
-    return ws.data_ptr(), ws.numel()
+        cuda = torch.device("cuda", idx)
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=cuda)
+        if idx not in _spare_workspaces:
+            # zero-filled now, handed to the first captures on new streams;
+            # the one-time wait makes the fill complete before any graph runs
+            _spare_workspaces[idx] = [torch.zeros(nbytes, dtype=torch.uint8, device=cuda)
+                                      for _ in range(_SPARE_WORKSPACES)]
+            torch.cuda.current_stream(cuda).synchronize()
+    _workspaces[key] = ws
+    return ws
 
 
 def _schedule(device: torch.device, lib, balanced: bool, grid_ctas: int) -> dict:
     _check(grid_ctas >= 0, "grid_ctas must be >= 0")
-    if not balanced:
+    ws = _workspace(device, lib) if balanced else None
+    if ws is None:
         return dict(workspace=None, workspace_bytes=0, grid_ctas=0)
-    ptr, nbytes = _workspace(device, lib)
-    return dict(workspace=ptr, workspace_bytes=nbytes, grid_ctas=int(grid_ctas))
+    return dict(workspace=ws.data_ptr(), workspace_bytes=ws.numel(), grid_ctas=int(grid_ctas))
 
 
 def _rows_operand(t: torch.Tensor, name: str) -> None:
@@ -174,13 +235,14 @@ def flexrel_attention(qkv: torch.Tensor, batch: int, heads: int, rel: torch.Tens
         kv_ptr = kv_len.data_ptr()
     _on_cuda(qkv, rel, out)
     dev = qkv.device
+    _raise_if_timed_out(dev)
     lib = N.load()
     with torch.cuda.device(dev):
         args = N.FdsFlexRelArgs(
             qkv=qkv.data_ptr(), qkv_row_stride=qkv.stride(0) if rows > 1 else width,
             rel=rel.data_ptr(), out=out.data_ptr(),
             out_row_stride=out.stride(0) if rows > 1 else hidden,
-            kv_len=kv_ptr, status=_status(dev).data_ptr(),
+            kv_len=kv_ptr, status=_status(dev).data_ptr(), status_host=_status_mirror(dev).data_ptr(),
             batch=batch, heads=heads, seq_len=length, head_dim=dim, dtype=_DTYPES[qkv.dtype],
             scale=1.0 / math.sqrt(dim), timeout_ns=int(timeout_ns), debug_flags=int(debug_flags),
             **_schedule(dev, lib, balanced and kv_len is None, grid_ctas),
@@ -199,9 +261,13 @@ def flexrel_attention_split(qkv: torch.Tensor, batch: int, heads: int, rel: torc
 
 
 def cudnn_attention_available(device=None) -> bool:
-    """Kept for ``model.py:89``; the B200 path needs no cuDNN, so this only
-    reports whether the device can run these kernels (sm_100)."""
-    return torch.cuda.is_available() and torch.cuda.get_device_capability(device) == (10, 0)
+    """Same meaning as the reference (``kernels.py:667-671``): whether cuDNN
+    SDPA (sm80+ with a cuDNN build) is available, which the reference's model
+    uses to choose its split path (``model.py:89``). This library's attention
+    does not use cuDNN; :func:`encoder_attention` ignores the choice."""
+    if not torch.backends.cudnn.is_available():
+        return False
+    return torch.cuda.get_device_capability(device) >= (8, 0)
 
 
 def encoder_attention(qkv, batch, heads, rel, impl: str = "split", kv_len=None):
@@ -276,12 +342,14 @@ def rope_attention(qkv: torch.Tensor, batch: int, heads: int, cos: torch.Tensor,
                f"scratch must be a contiguous [{rows}, {2 * hid}] {qkv.dtype} tensor on {qkv.device}")
     _on_cuda(qkv, cos, sin, out, scratch)
     dev = qkv.device
+    _raise_if_timed_out(dev)
     lib = N.load()
     with torch.cuda.device(dev):
         args = N.FdsRopeArgs(
             qkv=qkv.data_ptr(), qkv_row_stride=qkv.stride(0) if rows > 1 else width,
             cos=cos.data_ptr(), sin=sin.data_ptr(), qk_scratch=scratch.data_ptr(), out=out.data_ptr(),
             out_row_stride=out.stride(0) if rows > 1 else hid, status=_status(dev).data_ptr(),
+            status_host=_status_mirror(dev).data_ptr(),
             batch=batch, heads=heads, seq_len=length, head_dim=HEAD_DIM, dtype=_DTYPES[qkv.dtype],
             scale=1.0 / math.sqrt(HEAD_DIM), timeout_ns=int(timeout_ns), debug_flags=int(debug_flags),
             **_schedule(dev, lib, balanced, grid_ctas),

@@ -28,6 +28,15 @@
  * different workspaces. NULL keeps one unit per CTA. The split is used only
  * without kv_len, and only where it shortens the launch (or always, when
  * grid_ctas > 0 asks for it and the shape allows it); fds_attn_schedule tells.
+ *
+ * Status mirror (optional): a kernel whose bounded wait expires ORs an
+ * FDS_STATUS_* bit into the device word *status and also stores its bits into
+ * *status_host, a word of mapped pinned host memory (cudaHostAlloc /
+ * cudaMallocHost; with unified addressing its host pointer is also its device
+ * address). The caller can then notice a timeout by reading that host word at
+ * any time, e.g. before its next call, without synchronising the device. The
+ * store is plain (not atomic across the PCIe link): concurrent failures may
+ * leave only some of their bits, but never zero.
  */
 #ifndef FDS_B200_H
 #define FDS_B200_H
@@ -38,7 +47,7 @@
 extern "C" {
 #endif
 
-#define FDS_ABI_VERSION 2
+#define FDS_ABI_VERSION 3
 
 #if defined(_WIN32)
 #define FDS_API __declspec(dllexport)
@@ -95,6 +104,7 @@ typedef struct FdsFlexRelArgs {
     void* workspace;          /* device, zero-filled once; or NULL (see "Workspace" above) */
     int64_t workspace_bytes;
     int32_t grid_ctas;        /* pieces of a split last wave; 0 = one per SM */
+    int32_t* status_host;     /* mapped pinned host word, or NULL (see "Status mirror" above) */
 } FdsFlexRelArgs;
 
 FDS_API int fds_flexrel_attn_fwd(const FdsFlexRelArgs* args, void* stream);
@@ -130,6 +140,7 @@ typedef struct FdsRopeArgs {
     void* workspace;          /* as in FdsFlexRelArgs */
     int64_t workspace_bytes;
     int32_t grid_ctas;
+    int32_t* status_host;     /* as in FdsFlexRelArgs */
 } FdsRopeArgs;
 
 FDS_API int fds_rope_attn_fwd(const FdsRopeArgs* args, void* stream);
@@ -152,7 +163,9 @@ FDS_API int fds_rope_split(const void* qkv, int64_t qkv_row_stride, const float*
  * must be NULL and batch*seq_len*2*heads*64
  * 16-bit values must fit in it (else FDS_ERR_INVALID_ARGUMENT). The first call
  * on a device resolves the array's address (make it before any stream
- * capture). All calls share the array: calls that overlap on the GPU race.
+ * capture) and caches it; the cached address does not survive
+ * cudaDeviceReset. The stream must belong to the current device. All calls
+ * share the array: calls that overlap on the GPU race.
  */
 #define FDS_ROPE_STATIC_SCRATCH_BYTES (20u * 1024u * 1024u)
 FDS_API int fds_rope_attn_fwd_static(const FdsRopeArgs* args, void* stream);

@@ -3,6 +3,7 @@
 Run once in a container where the reference checkout is importable:
 
     python tests/golden/make_golden.py /path/to/FastDialogueSidon
+    (or FDS_REFERENCE_ROOT=/path/to/FastDialogueSidon python tests/golden/make_golden.py)
 
 It imports the reference's own fp32 modules -- FlexRelSelfAttention with eager
 flex_attention (triton/src/fds_triton/reference/modeling.py:33-122),
@@ -176,4 +177,7 @@ def main(root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FDS_REFERENCE_ROOT")
+    if not root:
+        raise SystemExit("usage: make_golden.py <reference checkout> (or set FDS_REFERENCE_ROOT)")
+    main(root)

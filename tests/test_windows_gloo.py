@@ -46,10 +46,16 @@ def _worker(rank: int, world: int, port: int, n: int, mode: str, out_path: str):
             os._exit(3)                      # the rank dies between windows
         if rank == 1 and mode == "hang" and len(done) == 1:
             time.sleep(3600)                 # the rank stops making progress
+        if rank == 1 and mode == "slow_first" and not done:
+            time.sleep(4.0)                  # a healthy but slow first window (> dead_after_s)
         done.append(w)
         return _window_record(w)
 
-    runner = WindowRunner(store, rank, world, n, heartbeat_s=0.05, dead_after_s=1.5, deadline_s=60)
+    if rank == 1 and mode == "late_start":
+        time.sleep(4.0)                      # starts well after rank 0 (> dead_after_s)
+    runner = WindowRunner(store, rank, world, n, heartbeat_s=0.05, dead_after_s=1.5,
+                          window_timeout_s=2.5 if mode == "hang" else 30.0, start_grace_s=20.0,
+                          deadline_s=60)
     rep = runner.run(process)
     if rank == 0:
         with open(out_path, "w") as f:
@@ -96,3 +102,12 @@ def test_failed_rank_windows_are_rerun(tmp_path, mode):
     assert {int(k): v for k, v in rep["results"].items()} == pytest.approx({w: _window_record(w) for w in range(7)})
     if mode == "crash":
         assert procs[1].exitcode == 3
+
+
+@pytest.mark.parametrize("mode", ["slow_first", "late_start"])
+def test_slow_healthy_rank_is_not_failed(tmp_path, mode):
+    """No false positives: a rank whose first window outlasts dead_after_s, or
+    that joins late, keeps its windows (heartbeat thread / start grace)."""
+    rep, procs = _run(mode, tmp_path)
+    assert rep["failed"] == [] and rep["requeued"] == {}
+    assert {int(k): v for k, v in rep["results"].items()} == pytest.approx({w: _window_record(w) for w in range(7)})

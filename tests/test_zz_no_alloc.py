@@ -4,9 +4,12 @@ callback, a serving loop with a fixed memory plan). Its scratch is a static
 device array inside the library, so the caller passes only inputs and outputs.
 
 Checked through the C ABI against the regular entry point (which takes a
-caller-allocated scratch) on two calls in a row with different inputs, so
-stale contents of the shared static array would show. Tolerance as the rest of
-the suite: max-abs <= 2e-3 and SNR >= 55 dB.
+caller-allocated scratch) on calls in a row with different inputs and sizes,
+in both orders (small then large, large then small), so stale contents of the
+shared static array would show. Both entry points run the same kernels on the
+same inputs, so their outputs must be bit-identical (torch.equal); the suite's
+numeric tolerance (max-abs <= 2e-3, SNR >= 55 dB) is checked against the CPU
+oracle on top. The static call must not change torch's allocated memory.
 """
 
 import ctypes
@@ -33,12 +36,16 @@ def _args(qkv, cos, sin, out, scratch, B, L, H, status):
         dtype=N.FDS_DTYPE_FP16, scale=1.0 / math.sqrt(64), timeout_ns=0, debug_flags=0)
 
 
-def test_static_scratch_matches_allocating_entry_point(cuda_device):
+@pytest.mark.parametrize("order", ["small_then_large", "large_then_small"])
+def test_static_scratch_matches_allocating_entry_point(cuda_device, order):
     lib = N.load()
     stream = torch.cuda.current_stream(cuda_device).cuda_stream
     status = torch.zeros(4, dtype=torch.int32, device=cuda_device)
-    for call, (B, L, H, seed) in enumerate([(2, 1000, 12, 1), (1, 6000, 12, 2)]):
-        gen = torch.Generator().manual_seed(seed)
+    shapes = [(2, 1000, 12, 1), (1, 6000, 12, 2)]
+    if order == "large_then_small":
+        shapes = shapes[::-1]
+    for call, (B, L, H, seed) in enumerate(shapes):
+        gen = torch.Generator().manual_seed(seed + 10 * call)
         qkv = (torch.randn(B * L, 3 * H * 64, generator=gen) * 0.55).half().to(cuda_device)
         cos, sin = rope_tables(L, cuda_device)
         out_ref = torch.empty(B * L, H * 64, dtype=torch.float16, device=cuda_device)
@@ -46,12 +53,18 @@ def test_static_scratch_matches_allocating_entry_point(cuda_device):
         rc = lib.fds_rope_attn_fwd(ctypes.byref(_args(qkv, cos, sin, out_ref, scratch, B, L, H, status)), stream)
         assert rc == N.FDS_OK, N.last_error()
         out = torch.full_like(out_ref, float("nan"))
+        torch.cuda.synchronize(cuda_device)
+        before = torch.cuda.memory_allocated(cuda_device)
         rc = lib.fds_rope_attn_fwd_static(ctypes.byref(_args(qkv, cos, sin, out, None, B, L, H, status)), stream)
         assert rc == N.FDS_OK, N.last_error()
         torch.cuda.synchronize(cuda_device)
+        assert torch.cuda.memory_allocated(cuda_device) == before
         assert int(status[0]) == 0
-        ref, got = out_ref.float().cpu(), out.float().cpu()
-        assert O.max_abs(ref, got) <= MAX_ABS and O.snr_db(ref, got) >= MIN_SNR, call
+        assert torch.equal(out, out_ref), call
+        if L <= 1000:  # the CPU oracle on the small call (tolerance of the suite)
+            ref = O.rope_attention(qkv.cpu(), B, H, cos.cpu(), sin.cpu(), round_qk_to=torch.float16)
+            got = out.float().cpu()
+            assert O.max_abs(ref, got) <= MAX_ABS and O.snr_db(ref, got) >= MIN_SNR, call
 
 
 def test_static_scratch_rejects_oversized_calls(cuda_device):
@@ -64,6 +77,10 @@ def test_static_scratch_rejects_oversized_calls(cuda_device):
     rc = lib.fds_rope_attn_fwd_static(ctypes.byref(_args(qkv, cos, sin, out, None, B, L, H, status)), None)
     assert rc == N.FDS_ERR_INVALID_ARGUMENT
     assert b"static scratch" in lib.fds_last_error()
+    # a caller-provided scratch is refused, also for a shape within the limit
+    B, L = 1, 1000
+    qkv, out = qkv[:B * L], out[:B * L]
     scratch = torch.zeros(B * L, 2 * H * 64, dtype=torch.float16, device=cuda_device)
     rc = lib.fds_rope_attn_fwd_static(ctypes.byref(_args(qkv, cos, sin, out, scratch, B, L, H, status)), None)
-    assert rc == N.FDS_ERR_INVALID_ARGUMENT  # a caller-provided scratch is refused
+    assert rc == N.FDS_ERR_INVALID_ARGUMENT
+    assert b"qk_scratch = NULL" in lib.fds_last_error()
