@@ -14,6 +14,26 @@ from fastdialoguesidon_b200 import _native as N
 pytestmark = pytest.mark.gpu
 
 
+def _capture(fn):
+    """Captures fn() in a new graph; returns (graph, bytes torch.cuda.memory_allocated
+    grew by during the capture)."""
+    torch.cuda.synchronize()
+    before = torch.cuda.memory_allocated()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g, torch.cuda.memory_allocated() - before
+
+
+def _capture_overhead() -> int:
+    """What a capture itself may allocate (torch registers the default
+    generator's graph state, e.g.), measured on an empty graph."""
+    g, grew = _capture(lambda: None)
+    del g
+    return grew
+
+
 def _inputs(B, L, H, seed, device):
     g = torch.Generator().manual_seed(seed)
     qkv = torch.randn(B * L, 3 * H * 64, generator=g).half().to(device)
@@ -29,12 +49,13 @@ def test_flexrel_out_overload_in_graph_allocates_nothing(cuda_device, L):
     buf = torch.empty_like(eager)
     ret = torch.ops.fds.flexrel_attention(qkv, B, H, rel, out=buf)    # .out overload, eager
     assert ret.data_ptr() == buf.data_ptr() and torch.equal(buf, eager)
+    overhead = _capture_overhead()
+    # its own capture stream: no workspace there yet, a pre-zeroed spare is taken
+    g, grew = _capture(lambda: torch.ops.fds.flexrel_attention(qkv, B, H, rel, out=buf))
+    assert grew <= overhead, (grew, overhead)
+    buf.zero_()
     torch.cuda.synchronize()
     before = torch.cuda.memory_allocated(cuda_device)
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):   # its own capture stream: no workspace yet, a spare is taken
-        torch.ops.fds.flexrel_attention(qkv, B, H, rel, out=buf)
-    buf.zero_()
     for _ in range(2):
         g.replay()
     torch.cuda.synchronize()
@@ -54,17 +75,19 @@ def test_rope_out_overload_in_graph_allocates_nothing(cuda_device):
     scratch = torch.empty(B * L, 2 * H * 64, dtype=qkv.dtype, device=cuda_device)
     torch.ops.fds.rope_attention(qkv, B, H, cos, sin, out=buf, scratch=scratch)
     assert torch.equal(buf, eager)
+    overhead = _capture_overhead()
+    rets = []
+    g, grew = _capture(lambda: rets.append(
+        torch.ops.fds.rope_attention(qkv, B, H, cos, sin, out=buf, scratch=scratch)))
+    assert grew <= overhead, (grew, overhead)
+    buf.zero_()
     torch.cuda.synchronize()
     before = torch.cuda.memory_allocated(cuda_device)
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        ret = torch.ops.fds.rope_attention(qkv, B, H, cos, sin, out=buf, scratch=scratch)
-    buf.zero_()
     g.replay()
     torch.cuda.synchronize()
     assert torch.cuda.memory_allocated(cuda_device) == before
     F.check_status()
-    assert ret.data_ptr() == buf.data_ptr() and torch.equal(buf, eager)
+    assert rets[0].data_ptr() == buf.data_ptr() and torch.equal(buf, eager)
     del g
 
 
