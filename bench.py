@@ -77,6 +77,7 @@ def parse_args():
                     help="profiling case: W + K eager launches of one layer (encoder or DiT) at L=6000")
     ap.add_argument("--no-config3", action="store_true")
     ap.add_argument("--no-throughput", action="store_true")
+    ap.add_argument("--no-linear", action="store_true")
     return ap.parse_args()
 
 
@@ -489,6 +490,64 @@ def run_reference(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def linear_leg(device: torch.device, steps: int = 20) -> dict:
+    """The projections either side of the attention on this library's tcgen05
+    GEMM, at the config-2 / config-4 shapes (L = 6000): the encoder QKV
+    projection with bias, the DiT QKV projection with the RoPE epilogue, the
+    out-projection accumulated into the fp32 residual. Each timed eagerly with
+    CUDA events over `steps` launches after 3 warm-up launches; torch's F.linear
+    (cuBLAS) on the same operands beside it for context. Algorithmic FLOPs
+    2 M N K; frac against the measured cuBLAS bf16 burst peak."""
+    import torch.nn.functional as Fn
+
+    import fastdialoguesidon_b200 as F
+
+    g = torch.Generator(device=device).manual_seed(17)
+    peak, _ = measured_peak()
+
+    def timed(fn) -> float:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(device)
+        return e0.elapsed_time(e1) / steps
+
+    res = {}
+    cases = (("encoder_qkv", 1024, 3072, "store"), ("dit_qkv_rope", 768, 2304, "rope"),
+             ("encoder_out_accumulate", 1024, 1024, "accum"))
+    cos, sin = F.rope_tables(L_WINDOW, device)
+    for name, k, n, kind in cases:
+        x = torch.randn(L_WINDOW, k, generator=g, device=device).half()
+        w = (torch.randn(n, k, generator=g, device=device) * 0.02).half()
+        b = (torch.randn(n, generator=g, device=device) * 0.02).half()
+        flop = 2.0 * L_WINDOW * n * k
+        if kind == "store":
+            out = torch.empty(L_WINDOW, n, dtype=torch.float16, device=device)
+            ours = timed(lambda: F.linear(x, w, b, out=out))
+            ref = timed(lambda: Fn.linear(x, w, b))
+        elif kind == "rope":
+            out = torch.empty(L_WINDOW, n, dtype=torch.float16, device=device)
+            ours = timed(lambda: F.linear_rope(x, w, b, cos, sin, L_WINDOW, n // 192, out=out))
+            ref = timed(lambda: Fn.linear(x, w, b))
+        else:
+            acc = torch.zeros(L_WINDOW, n, device=device)
+            ours = timed(lambda: F.accumulate(acc, x, w))
+            ref = timed(lambda: torch.addmm(acc, x, w.t(), out_dtype=torch.float32, out=acc))
+        tf = flop / (ours * 1e-3) / 1e12
+        res[name] = {"m": L_WINDOW, "n": n, "k": k, "ms": round(ours, 4), "tflops": round(tf, 1),
+                     "frac": round(tf / peak, 3), "torch_ms": round(ref, 4),
+                     "torch_tflops": round(flop / (ref * 1e-3) / 1e12, 1)}
+    F.check_status(device)
+    res["note"] = ("tcgen05 GEMM of this library (fds_linear_fwd); torch_ms: torch.nn.functional.linear / "
+                   "torch.addmm (cuBLAS) on the same operands, the reference's own call at these sites")
+    return res
+
+
 def config3_leg(args, rank: int, device: torch.device, dist_on: bool, bal: bool) -> dict:
     """Config 3: a batch of 8 windows of seeded random length, bucketed to 10 s,
     padded to the longest bucket, keys masked past each window's true length
@@ -671,6 +730,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                                 / (sweep_ms * 1e-3) / 1e12, 1),
                 "steps": tp["steps"], "clocks_rank0": tp["clocks"],
                 "timing": "one CUDA graph per rank per sweep; max over ranks of the device time"}
+        if world == 1 and not args.no_linear:
+            line["linear"] = linear_leg(device)
         if world == 1 and not args.no_cpu_baseline:
             cms, info = cpu_layer_ms_per_window(threads=os.cpu_count())
             line["cpu_baseline"] = {"value": round(cms, 1), "unit": UNIT, "cores": info["cores"],

@@ -30,6 +30,10 @@ FDS_DEBUG_FORCE_TIMEOUT = 0x1
 
 FDS_ROPE_STATIC_SCRATCH_BYTES = 20 * 1024 * 1024
 
+FDS_EPILOGUE_STORE = 0
+FDS_EPILOGUE_ROPE = 1
+FDS_EPILOGUE_ACCUMULATE_F32 = 2
+
 ABI_VERSION = 3
 
 # every symbol include/fds_b200.h declares (checked by the CPU test suite)
@@ -43,6 +47,7 @@ EXPORTED_SYMBOLS = (
     "fds_attn_smem_bytes",
     "fds_attn_workspace_bytes",
     "fds_attn_schedule",
+    "fds_linear_fwd",
 )
 
 
@@ -92,6 +97,32 @@ class FdsRopeArgs(ctypes.Structure):
         ("workspace_bytes", ctypes.c_int64),
         ("grid_ctas", ctypes.c_int32),
         ("status_host", ctypes.c_void_p),
+        ("qk_rotated", ctypes.c_int32),
+    ]
+
+
+class FdsLinearArgs(ctypes.Structure):
+    _fields_ = [
+        ("a", ctypes.c_void_p),
+        ("a_row_stride", ctypes.c_int64),
+        ("w", ctypes.c_void_p),
+        ("w_row_stride", ctypes.c_int64),
+        ("bias", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("out_row_stride", ctypes.c_int64),
+        ("cos", ctypes.c_void_p),
+        ("sin", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
+        ("status_host", ctypes.c_void_p),
+        ("m", ctypes.c_int32),
+        ("n", ctypes.c_int32),
+        ("k", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("epilogue", ctypes.c_int32),
+        ("seq_len", ctypes.c_int32),
+        ("rope_cols", ctypes.c_int32),
+        ("timeout_ns", ctypes.c_int64),
+        ("grid_ctas", ctypes.c_int32),
     ]
 
 
@@ -123,6 +154,8 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         lib.fds_rope_attn_fwd.restype = ctypes.c_int
         lib.fds_rope_attn_fwd_static.argtypes = [ctypes.POINTER(FdsRopeArgs), ctypes.c_void_p]
         lib.fds_rope_attn_fwd_static.restype = ctypes.c_int
+        lib.fds_linear_fwd.argtypes = [ctypes.POINTER(FdsLinearArgs), ctypes.c_void_p]
+        lib.fds_linear_fwd.restype = ctypes.c_int
         lib.fds_rope_split.argtypes = [
             ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
             ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,

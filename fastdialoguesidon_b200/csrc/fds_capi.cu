@@ -17,6 +17,7 @@
 #include "attn_kernel.cuh"
 #include "capi_internal.h"
 #include "fds_b200.h"
+#include "gemm_kernel.cuh"
 #include "rope.cuh"
 
 namespace {
@@ -116,6 +117,26 @@ int make_rel_map(CUtensorMap* map, const void* base, int dtype) {
                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(FDS_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled(rel) failed (%d)", static_cast<int>(r));
+    return FDS_OK;
+}
+
+// 2-D map over a [rows, cols] row-major matrix (row stride `row_stride`
+// elements), box 64 columns x `box_rows` rows, 128-byte swizzle, zero fill
+// past the last row.
+int make_matrix_map(CUtensorMap* map, const void* base, int dtype, int64_t cols, int64_t rows, int64_t row_stride,
+                    int box_rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (enc == nullptr) return fail(FDS_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled unavailable from the driver");
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride * 2)};
+    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapDataType dt =
+        dtype == FDS_DTYPE_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(FDS_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled(matrix) failed (%d)", static_cast<int>(r));
     return FDS_OK;
 }
 
@@ -289,6 +310,46 @@ int fds_detail::set_error(int code, const char* fmt, ...) {
     return code;
 }
 
+namespace {
+
+template <typename T, int BN, int kEpi>
+int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const fds::gemm::Params& p, int grid,
+                cudaStream_t stream) {
+    auto kern = fds::gemm::gemm_kernel<T, BN, kEpi>;
+    constexpr int smem = fds::gemm::Smem<BN>::alloc;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "cudaFuncSetAttribute(gemm): %s", cudaGetErrorString(e));
+    e = launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(fds::gemm::kThreads), smem, stream, ma, mb, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "linear launch: %s", cudaGetErrorString(e));
+    return FDS_OK;
+}
+
+template <typename T, int BN>
+int launch_gemm_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const fds::gemm::Params& p, int grid,
+                    cudaStream_t stream) {
+    switch (epi) {
+        case FDS_EPILOGUE_STORE: return launch_gemm<T, BN, fds::gemm::kStore>(ma, mb, p, grid, stream);
+        case FDS_EPILOGUE_ROPE: return launch_gemm<T, BN, fds::gemm::kRope>(ma, mb, p, grid, stream);
+        default: return launch_gemm<T, BN, fds::gemm::kAccum>(ma, mb, p, grid, stream);
+    }
+}
+
+// Output tile width: 256 columns (more reuse of each A tile) unless n is not a
+// multiple of 256 or 128-column tiles fill the last wave clearly better.
+int choose_bn(int64_t m, int64_t n, int64_t ctas) {
+    if (n % 256 != 0) return 128;
+    const int64_t mt = (m + fds::gemm::kBM - 1) / fds::gemm::kBM;
+    const auto fill = [&](int64_t bn) {
+        const int64_t tiles = mt * (n / bn);
+        const int64_t waves = (tiles + ctas - 1) / ctas;
+        return static_cast<double>(tiles) / static_cast<double>(waves * ctas);
+    };
+    return fill(128) > fill(256) + 0.1 ? 128 : 256;
+}
+
+}  // namespace
+
 extern "C" {
 
 int fds_abi_version(void) { return FDS_ABI_VERSION; }
@@ -393,10 +454,13 @@ int fds_rope_attn_fwd(const FdsRopeArgs* a, void* stream) {
     int rc = check_common(a->qkv, a->qkv_row_stride, a->out, a->out_row_stride, a->batch, a->heads, a->seq_len,
                           a->head_dim, a->dtype);
     if (rc != FDS_OK) return rc;
-    if (a->cos == nullptr || a->sin == nullptr || !aligned16(a->cos) || !aligned16(a->sin))
-        return fail(FDS_ERR_INVALID_ARGUMENT, "cos/sin must be 16-byte aligned fp32 [>= seq_len, 64] tables");
-    if (a->qk_scratch == nullptr || !aligned16(a->qk_scratch))
-        return fail(FDS_ERR_INVALID_ARGUMENT, "qk_scratch must be a 16-byte aligned [batch*seq_len, 2*heads*64] buffer");
+    if (!a->qk_rotated) {
+        if (a->cos == nullptr || a->sin == nullptr || !aligned16(a->cos) || !aligned16(a->sin))
+            return fail(FDS_ERR_INVALID_ARGUMENT, "cos/sin must be 16-byte aligned fp32 [>= seq_len, 64] tables");
+        if (a->qk_scratch == nullptr || !aligned16(a->qk_scratch))
+            return fail(FDS_ERR_INVALID_ARGUMENT,
+                        "qk_scratch must be a 16-byte aligned [batch*seq_len, 2*heads*64] buffer");
+    }
     if (!(a->scale > 0.f)) return fail(FDS_ERR_INVALID_ARGUMENT, "scale must be > 0");
     if ((rc = check_device()) != FDS_OK) return rc;
 
@@ -404,17 +468,21 @@ int fds_rope_attn_fwd(const FdsRopeArgs* a, void* stream) {
     const int64_t rows = static_cast<int64_t>(a->batch) * a->seq_len;
     if (rows > 0x7fffffffLL) return fail(FDS_ERR_INVALID_ARGUMENT, "batch*seq_len too large");
     CUtensorMap mqk, mv;
-    if ((rc = make_rows_map(&mqk, a->qk_scratch, a->dtype, 2 * hid, a->seq_len, a->batch, 2 * hid, fds::kBlockM)) !=
-        FDS_OK)
-        return rc;
     if ((rc = make_rows_map(&mv, a->qkv, a->dtype, 3 * hid, a->seq_len, a->batch, a->qkv_row_stride, fds::kBlockM)) !=
         FDS_OK)
         return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    char* scratch = static_cast<char*>(a->qk_scratch);
-    rc = launch_rope(a->qkv, a->qkv_row_stride, a->cos, a->sin, scratch, scratch + hid * 2, nullptr, 2 * hid,
-                     static_cast<int>(rows), a->seq_len, a->heads, a->dtype, s);
-    if (rc != FDS_OK) return rc;
+    if (a->qk_rotated) {
+        mqk = mv;  // q | k read rotated straight from qkv
+    } else {
+        if ((rc = make_rows_map(&mqk, a->qk_scratch, a->dtype, 2 * hid, a->seq_len, a->batch, 2 * hid,
+                                fds::kBlockM)) != FDS_OK)
+            return rc;
+        char* scratch = static_cast<char*>(a->qk_scratch);
+        rc = launch_rope(a->qkv, a->qkv_row_stride, a->cos, a->sin, scratch, scratch + hid * 2, nullptr, 2 * hid,
+                         static_cast<int>(rows), a->seq_len, a->heads, a->dtype, s);
+        if (rc != FDS_OK) return rc;
+    }
 
     fds::AttnParams p{};
     p.out = a->out;
@@ -433,6 +501,71 @@ int fds_rope_attn_fwd(const FdsRopeArgs* a, void* stream) {
     const Workspace ws{a->workspace, a->workspace_bytes, a->grid_ctas};
     rc = a->dtype == FDS_DTYPE_FP16 ? launch_attn<__half, false>(mqk, mqk, mv, mqk, p, a->batch, ws, s)
                                     : launch_attn<__nv_bfloat16, false>(mqk, mqk, mv, mqk, p, a->batch, ws, s);
+    return rc == FDS_OK ? ok() : rc;
+}
+
+int fds_linear_fwd(const FdsLinearArgs* a, void* stream) {
+    if (a == nullptr) return fail(FDS_ERR_INVALID_ARGUMENT, "null args");
+    if (a->a == nullptr || a->w == nullptr || a->out == nullptr)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "null a/w/out pointer");
+    if (a->dtype != FDS_DTYPE_FP16 && a->dtype != FDS_DTYPE_BF16)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "dtype must be FDS_DTYPE_FP16 or FDS_DTYPE_BF16 (got %d)", a->dtype);
+    if (a->epilogue < FDS_EPILOGUE_STORE || a->epilogue > FDS_EPILOGUE_ACCUMULATE_F32)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "unknown epilogue %d", a->epilogue);
+    if (a->m < 1 || a->n < 1 || a->k < 1) return fail(FDS_ERR_INVALID_ARGUMENT, "m, n, k must be >= 1");
+    if (a->k % 64 != 0) return fail(FDS_ERR_INVALID_ARGUMENT, "k must be a multiple of 64 (got %d)", a->k);
+    if (a->n % 128 != 0) return fail(FDS_ERR_INVALID_ARGUMENT, "n must be a multiple of 128 (got %d)", a->n);
+    if (a->a_row_stride < a->k || a->a_row_stride % 8 != 0 || a->w_row_stride < a->k || a->w_row_stride % 8 != 0)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "a / w row strides must be >= k and multiples of 8 elements");
+    const bool f32_out = a->epilogue == FDS_EPILOGUE_ACCUMULATE_F32;
+    if (a->out_row_stride < a->n || a->out_row_stride % (f32_out ? 4 : 8) != 0)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "out row stride must be >= n and 16-byte aligned rows");
+    if (!aligned16(a->a) || !aligned16(a->w) || !aligned16(a->out) || (a->bias != nullptr && !aligned16(a->bias)))
+        return fail(FDS_ERR_INVALID_ARGUMENT, "a, w, bias and out must be 16-byte aligned");
+    if (a->epilogue == FDS_EPILOGUE_ROPE) {
+        if (a->cos == nullptr || a->sin == nullptr || !aligned16(a->cos) || !aligned16(a->sin))
+            return fail(FDS_ERR_INVALID_ARGUMENT, "cos/sin must be 16-byte aligned fp32 [>= seq_len, 64] tables");
+        if (a->seq_len < 1) return fail(FDS_ERR_INVALID_ARGUMENT, "seq_len must be >= 1");
+        if (a->rope_cols < 0 || a->rope_cols > a->n || a->rope_cols % 64 != 0)
+            return fail(FDS_ERR_INVALID_ARGUMENT, "rope_cols must be a multiple of 64 in [0, n]");
+    }
+    int rc = check_device();
+    if (rc != FDS_OK) return rc;
+    const int sms = sm_count();
+    if (a->grid_ctas < 0 || (a->grid_ctas > 0 && sms > 0 && a->grid_ctas > sms))
+        return fail(FDS_ERR_INVALID_ARGUMENT, "grid_ctas must be in [0, %d] (got %d)", sms, a->grid_ctas);
+    const int64_t ctas = a->grid_ctas > 0 ? a->grid_ctas : (sms > 0 ? sms : 148);
+    const int bn = choose_bn(a->m, a->n, ctas);
+    const int64_t tiles = static_cast<int64_t>((a->m + fds::gemm::kBM - 1) / fds::gemm::kBM) * (a->n / bn);
+    if (tiles > 0x7fffffffLL) return fail(FDS_ERR_INVALID_ARGUMENT, "too many tiles");
+
+    CUtensorMap ma, mb;
+    if ((rc = make_matrix_map(&ma, a->a, a->dtype, a->k, a->m, a->a_row_stride, fds::gemm::kBM)) != FDS_OK) return rc;
+    if ((rc = make_matrix_map(&mb, a->w, a->dtype, a->k, a->n, a->w_row_stride, bn)) != FDS_OK) return rc;
+    fds::gemm::Params p{};
+    p.out = a->out;
+    p.out_stride = a->out_row_stride;
+    p.bias = a->bias;
+    p.cos_t = a->cos;
+    p.sin_t = a->sin;
+    p.status = a->status;
+    p.status_host = a->status_host;
+    p.timeout_ns = a->timeout_ns;
+    p.m = a->m;
+    p.n = a->n;
+    p.k = a->k;
+    p.seq_len = a->seq_len;
+    p.rope_cols = a->epilogue == FDS_EPILOGUE_ROPE ? a->rope_cols : 0;
+    p.tiles_n = a->n / bn;
+    p.tiles = static_cast<int32_t>(tiles);
+    const int grid = static_cast<int>(tiles < ctas ? tiles : ctas);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (a->dtype == FDS_DTYPE_FP16)
+        rc = bn == 256 ? launch_gemm_epi<__half, 256>(a->epilogue, ma, mb, p, grid, s)
+                       : launch_gemm_epi<__half, 128>(a->epilogue, ma, mb, p, grid, s);
+    else
+        rc = bn == 256 ? launch_gemm_epi<__nv_bfloat16, 256>(a->epilogue, ma, mb, p, grid, s)
+                       : launch_gemm_epi<__nv_bfloat16, 128>(a->epilogue, ma, mb, p, grid, s);
     return rc == FDS_OK ? ok() : rc;
 }
 

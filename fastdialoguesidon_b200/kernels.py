@@ -359,6 +359,130 @@ def rope_attention(qkv: torch.Tensor, batch: int, heads: int, cos: torch.Tensor,
     return out
 
 
+def rotated_attention(qkv: torch.Tensor, batch: int, heads: int, out: torch.Tensor | None = None,
+                      *, timeout_ns: int = 0, debug_flags: int = 0, balanced: bool = True,
+                      grid_ctas: int = 0) -> torch.Tensor:
+    """Bidirectional softmax(q k^T / 8) v over a qkv [B*L, 3*HID] whose q | k
+    column blocks are rotated already (the :func:`linear_rope` output): the DiT
+    attention with no RoPE pass and no scratch. -> [B*L, HID]."""
+    _rows_operand(qkv, "qkv")
+    rows, width = qkv.shape
+    _check(batch >= 1 and heads >= 1, "batch and heads must be >= 1")
+    _check(width % 3 == 0, "qkv width is not 3 * hidden")
+    hid = width // 3
+    _check(hid % heads == 0 and hid // heads == HEAD_DIM, "head_dim must be 64")
+    _check(rows % batch == 0 and rows > 0, f"rows {rows} not a positive multiple of batch {batch}")
+    length = rows // batch
+    if out is None:
+        out = torch.empty(rows, hid, device=qkv.device, dtype=qkv.dtype)
+    else:
+        _rows_operand(out, "out")
+        _check(out.shape == (rows, hid) and out.dtype == qkv.dtype and out.device == qkv.device,
+               f"out must be a [{rows}, {hid}] {qkv.dtype} tensor on {qkv.device}")
+    _on_cuda(qkv, out)
+    dev = qkv.device
+    _raise_if_timed_out(dev)
+    lib = N.load()
+    with torch.cuda.device(dev):
+        args = N.FdsRopeArgs(
+            qkv=qkv.data_ptr(), qkv_row_stride=qkv.stride(0) if rows > 1 else width,
+            cos=None, sin=None, qk_scratch=None, out=out.data_ptr(),
+            out_row_stride=out.stride(0) if rows > 1 else hid, status=_status(dev).data_ptr(),
+            status_host=_status_mirror(dev).data_ptr(), qk_rotated=1,
+            batch=batch, heads=heads, seq_len=length, head_dim=HEAD_DIM, dtype=_DTYPES[qkv.dtype],
+            scale=1.0 / math.sqrt(HEAD_DIM), timeout_ns=int(timeout_ns), debug_flags=int(debug_flags),
+            **_schedule(dev, lib, balanced, grid_ctas),
+        )
+        rc = lib.fds_rope_attn_fwd(ctypes.byref(args), _stream_ptr(dev))
+    _raise_rc(rc, "fds_rope_attn_fwd")
+    return out
+
+
+def _linear_call(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, out: torch.Tensor,
+                 epilogue: int, cos=None, sin=None, seq_len: int = 0, rope_cols: int = 0,
+                 timeout_ns: int = 0, grid_ctas: int = 0) -> torch.Tensor:
+    _rows_operand(x, "x")
+    _rows_operand(w, "w")
+    m, k = x.shape
+    n, kw = w.shape
+    _check(kw == k, f"w is [{n}, {kw}] but x has {k} columns")
+    _check(w.dtype == x.dtype and w.device == x.device, "w must match x's dtype and device")
+    _check(k % 64 == 0, f"in_features must be a multiple of 64 (got {k})")
+    _check(n % 128 == 0, f"out_features must be a multiple of 128 (got {n})")
+    if bias is not None:
+        _check(isinstance(bias, torch.Tensor) and bias.shape == (n,) and bias.is_contiguous()
+               and bias.dtype == x.dtype and bias.device == x.device and bias.data_ptr() % 16 == 0,
+               f"bias must be a contiguous [{n}] {x.dtype} tensor on {x.device}")
+    _on_cuda(x, w, out)
+    dev = x.device
+    _raise_if_timed_out(dev)
+    lib = N.load()
+    with torch.cuda.device(dev):
+        args = N.FdsLinearArgs(
+            a=x.data_ptr(), a_row_stride=x.stride(0) if m > 1 else k, w=w.data_ptr(),
+            w_row_stride=w.stride(0) if n > 1 else k, bias=None if bias is None else bias.data_ptr(),
+            out=out.data_ptr(), out_row_stride=out.stride(0) if m > 1 else n,
+            cos=None if cos is None else cos.data_ptr(), sin=None if sin is None else sin.data_ptr(),
+            status=_status(dev).data_ptr(), status_host=_status_mirror(dev).data_ptr(),
+            m=m, n=n, k=k, dtype=_DTYPES[x.dtype], epilogue=epilogue, seq_len=int(seq_len),
+            rope_cols=int(rope_cols), timeout_ns=int(timeout_ns), grid_ctas=int(grid_ctas))
+        rc = lib.fds_linear_fwd(ctypes.byref(args), _stream_ptr(dev))
+    _raise_rc(rc, "fds_linear_fwd")
+    return out
+
+
+def _linear_out(x: torch.Tensor, n: int, out: torch.Tensor | None, dtype) -> torch.Tensor:
+    m = x.shape[0]
+    if out is None:
+        return torch.empty(m, n, device=x.device, dtype=dtype)
+    _rows_operand(out, "out") if dtype != torch.float32 else None
+    _check(out.shape == (m, n) and out.dtype == dtype and out.device == x.device and out.stride(1) == 1,
+           f"out must be a [{m}, {n}] {dtype} tensor on {x.device} with contiguous rows")
+    return out
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None,
+           out: torch.Tensor | None = None, *, grid_ctas: int = 0) -> torch.Tensor:
+    """``F.linear(x, w, b)`` on the tensor cores: x [M, K], w [N, K] (nn.Linear
+    layout), fp16 / bf16, fp32 accumulation, result rounded once to x's dtype.
+    Reference: ``linear`` (triton/src/fds_triton/model.py:50-51), used for the
+    QKV projection before the attention (model.py:289)."""
+    out = _linear_out(x, w.shape[0], out, x.dtype)
+    return _linear_call(x, w, b, out, N.FDS_EPILOGUE_STORE, grid_ctas=grid_ctas)
+
+
+def linear_rope(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, cos: torch.Tensor,
+                sin: torch.Tensor, length: int, heads: int, out: torch.Tensor | None = None,
+                *, grid_ctas: int = 0) -> torch.Tensor:
+    """The DiT's QKV projection with RoPE in its epilogue: ``F.linear(x, w, b)``
+    (rounded to x's dtype) followed by ``rope_split``'s rotation of the q and k
+    column blocks (position = row % length), written as one [M, 3*heads*64]
+    tensor that :func:`rotated_attention` reads directly. Replaces
+    triton/src/fds_triton/model.py:318-319 (linear + K.rope_split)."""
+    n = w.shape[0]
+    _check(n == 3 * heads * HEAD_DIM, f"w must have 3*heads*64 = {3 * heads * HEAD_DIM} rows (got {n})")
+    _check(length >= 1, "length must be >= 1")
+    _rope_tables(cos, sin, min(length, x.shape[0]), x)
+    out = _linear_out(x, n, out, x.dtype)
+    return _linear_call(x, w, b, out, N.FDS_EPILOGUE_ROPE, cos=cos, sin=sin, seq_len=length,
+                        rope_cols=2 * heads * HEAD_DIM, grid_ctas=grid_ctas)
+
+
+def accumulate(x: torch.Tensor, a: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None,
+               *, grid_ctas: int = 0) -> None:
+    """``x += a @ w.T`` in place: fp16 / bf16 operands, fp32 accumulation added
+    straight into the fp32 residual x (no reduced-precision GEMM output, no
+    separate add). Reference: ``accumulate`` (triton/src/fds_triton/model.py:
+    53-57, ``torch.addmm(x, a, w.t(), out_dtype=torch.float32, out=x)``), the
+    attention's out-projection (model.py:291)."""
+    _check(isinstance(x, torch.Tensor) and x.dtype == torch.float32 and x.dim() == 2,
+           "x must be a 2-D fp32 tensor (the residual stream)")
+    _check(x.stride(1) == 1 and (x.shape[0] <= 1 or x.stride(0) % 4 == 0) and x.data_ptr() % 16 == 0,
+           "x rows must be contiguous and 16-byte aligned")
+    _check(x.shape == (a.shape[0], w.shape[0]), f"x must be [{a.shape[0]}, {w.shape[0]}], got {tuple(x.shape)}")
+    _linear_call(a, w, b, x, N.FDS_EPILOGUE_ACCUMULATE_F32, grid_ctas=grid_ctas)
+
+
 def rope_tables(max_seq: int, device=None, dim: int = HEAD_DIM, base: float = 10000.0):
     """fp32 cos/sin [max_seq, dim] tables as the reference builds them
     (model.py:201-205: inv_freq = base^(-arange(0, dim/2)/(dim/2)), cat([f, f]))."""

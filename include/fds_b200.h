@@ -141,6 +141,9 @@ typedef struct FdsRopeArgs {
     int64_t workspace_bytes;
     int32_t grid_ctas;
     int32_t* status_host;     /* as in FdsFlexRelArgs */
+    int32_t qk_rotated;       /* non-zero: the q | k columns of qkv are rotated already (the
+                                 FDS_EPILOGUE_ROPE output of fds_linear_fwd): no RoPE pass,
+                                 cos / sin / qk_scratch unused (may be NULL) */
 } FdsRopeArgs;
 
 FDS_API int fds_rope_attn_fwd(const FdsRopeArgs* args, void* stream);
@@ -169,6 +172,52 @@ FDS_API int fds_rope_split(const void* qkv, int64_t qkv_row_stride, const float*
  */
 #define FDS_ROPE_STATIC_SCRATCH_BYTES (20u * 1024u * 1024u)
 FDS_API int fds_rope_attn_fwd_static(const FdsRopeArgs* args, void* stream);
+
+/*
+ * Linear layer on the tensor cores, D = A W^T with W in nn.Linear's [n, k]
+ * layout, fp16 / bf16 operands, fp32 accumulation, and one epilogue:
+ *   FDS_EPILOGUE_STORE          out[m, n] (dtype) = D + bias
+ *   FDS_EPILOGUE_ROPE           out = D + bias rounded to dtype, then the DiT's
+ *                               rotate-half RoPE (cos / sin fp32 [>= seq_len, 64],
+ *                               position = row % seq_len) on every 64-column head
+ *                               of columns [0, rope_cols), rounded again: the q | k
+ *                               the attention reads, with no separate RoPE pass
+ *   FDS_EPILOGUE_ACCUMULATE_F32 out[m, n] (fp32) += D (+ bias): the residual
+ *                               update x += a W^T
+ * k must be a multiple of 64 and n of 128; rows past m are not written.
+ * Replaces: the projections around the attention, triton/src/fds_triton/model.py
+ * :289 (qkv = linear(xn, qkv_w, qkv_b), encoder), :318 (DiT qkv, followed by
+ * rope_split :319), :291 and accumulate :53-57 (x += ctx out_w^T into the fp32
+ * residual).
+ */
+#define FDS_EPILOGUE_STORE 0
+#define FDS_EPILOGUE_ROPE 1
+#define FDS_EPILOGUE_ACCUMULATE_F32 2
+
+typedef struct FdsLinearArgs {
+    const void* a;            /* device, dtype, [m, a_row_stride] */
+    int64_t a_row_stride;     /* elements; multiple of 8, >= k */
+    const void* w;            /* device, dtype, [n, w_row_stride] */
+    int64_t w_row_stride;     /* elements; multiple of 8, >= k */
+    const void* bias;         /* device, dtype, [n], or NULL */
+    void* out;                /* device, [m, out_row_stride]: dtype, or fp32 for ACCUMULATE_F32 */
+    int64_t out_row_stride;   /* elements; multiple of 8 (4 for fp32), >= n */
+    const float* cos;         /* FDS_EPILOGUE_ROPE only */
+    const float* sin;
+    int32_t* status;          /* device word for bounded-wait errors, or NULL */
+    int32_t* status_host;     /* mapped pinned host mirror, or NULL */
+    int32_t m;                /* rows of a and out */
+    int32_t n;                /* rows of w, columns of out */
+    int32_t k;                /* columns of a and w */
+    int32_t dtype;            /* FDS_DTYPE_* of a, w, bias (and out, unless ACCUMULATE_F32) */
+    int32_t epilogue;         /* FDS_EPILOGUE_* */
+    int32_t seq_len;          /* FDS_EPILOGUE_ROPE: frames per window */
+    int32_t rope_cols;        /* FDS_EPILOGUE_ROPE: multiple of 64, <= n */
+    int64_t timeout_ns;       /* bound on every in-kernel wait; <= 0 selects 2 s */
+    int32_t grid_ctas;        /* persistent CTAs; 0 = one per SM */
+} FdsLinearArgs;
+
+FDS_API int fds_linear_fwd(const FdsLinearArgs* args, void* stream);
 
 /* Version of this ABI (FDS_ABI_VERSION). */
 FDS_API int fds_abi_version(void);

@@ -35,7 +35,8 @@ def test_library_exports_every_declared_symbol():
 
 def test_struct_layouts_match_header():
     text = HEADER.read_text()
-    for struct, cls in (("FdsFlexRelArgs", N.FdsFlexRelArgs), ("FdsRopeArgs", N.FdsRopeArgs)):
+    for struct, cls in (("FdsFlexRelArgs", N.FdsFlexRelArgs), ("FdsRopeArgs", N.FdsRopeArgs),
+                        ("FdsLinearArgs", N.FdsLinearArgs)):
         body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (struct, struct), text, re.S).group(1)
         fields = re.findall(r"^\s*[\w\s\*]+?\b(\w+);", body, re.M)
         assert fields == [f[0] for f in cls._fields_], (struct, fields)
@@ -68,6 +69,47 @@ def test_c_abi_rope_split_rejects_invalid_arguments():
     assert rc == N.FDS_ERR_INVALID_ARGUMENT
     rc = lib.fds_rope_split(16, 2300, 16, 16, 16, 10, 10, 12, 64, N.FDS_DTYPE_FP16, None)
     assert rc == N.FDS_ERR_INVALID_ARGUMENT
+
+
+def _linear_args(**kw):
+    base = dict(a=16, a_row_stride=1024, w=16, w_row_stride=1024, bias=None, out=16, out_row_stride=3072,
+                cos=None, sin=None, status=None, status_host=None, m=6000, n=3072, k=1024,
+                dtype=N.FDS_DTYPE_FP16, epilogue=N.FDS_EPILOGUE_STORE, seq_len=0, rope_cols=0, timeout_ns=0,
+                grid_ctas=0)
+    base.update(kw)
+    return N.FdsLinearArgs(**base)
+
+
+@pytest.mark.parametrize("bad", [
+    dict(k=1000, a_row_stride=1000, w_row_stride=1000), dict(n=3000, out_row_stride=3000), dict(m=0),
+    dict(dtype=5), dict(epilogue=9), dict(a=0), dict(w=0), dict(out=0), dict(a=24), dict(bias=8),
+    dict(a_row_stride=1000), dict(out_row_stride=3000), dict(epilogue=N.FDS_EPILOGUE_ROPE, seq_len=100),
+    dict(epilogue=N.FDS_EPILOGUE_ROPE, cos=16, sin=16, seq_len=0, rope_cols=128),
+    dict(epilogue=N.FDS_EPILOGUE_ROPE, cos=16, sin=16, seq_len=100, rope_cols=100),
+    dict(epilogue=N.FDS_EPILOGUE_ROPE, cos=16, sin=16, seq_len=100, rope_cols=4096),
+    dict(epilogue=N.FDS_EPILOGUE_ACCUMULATE_F32, out_row_stride=3070),
+])
+def test_c_abi_linear_rejects_invalid_arguments_before_launch(bad):
+    lib = N.load()
+    rc = lib.fds_linear_fwd(ctypes.byref(_linear_args(**bad)), None)
+    assert rc == N.FDS_ERR_INVALID_ARGUMENT, bad
+    assert lib.fds_last_error()
+    assert lib.fds_linear_fwd(None, None) == N.FDS_ERR_INVALID_ARGUMENT
+
+
+def test_linear_validation():
+    x = torch.zeros(100, 1024, dtype=torch.float16)
+    w = torch.zeros(3072, 1024, dtype=torch.float16)
+    with pytest.raises(F.FdsError):
+        F.linear(x, torch.zeros(3072, 1000, dtype=torch.float16))        # in_features mismatch
+    with pytest.raises(F.FdsError):
+        F.linear(x[:, :1000], torch.zeros(3072, 1000, dtype=torch.float16))  # k not a multiple of 64
+    with pytest.raises(F.FdsError):
+        F.linear(x, w, torch.zeros(3071, dtype=torch.float16))           # bias shape
+    with pytest.raises(F.FdsError):
+        F.accumulate(torch.zeros(100, 3072, dtype=torch.float16), x, w)  # residual must be fp32
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        F.linear(x, w)                                                  # valid shapes, CPU tensors
 
 
 def test_op_validation_mirrors_reference_asserts():
