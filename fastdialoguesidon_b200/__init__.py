@@ -4,6 +4,8 @@ Public API (mirrors the attention ops of ``fds_triton.kernels``):
 
 - :func:`flexrel_attention` / :func:`flexrel_attention_split` /
   :func:`encoder_attention`: w2v-BERT relative_key self-attention;
+  :func:`flexrel_attention_qr`: the same with q, k, v and q.rel^T given
+  separately, in the TensorRT plugin's [B, L, H, D] layout;
 - :func:`rope_attention`: the DiT head's RoPE self-attention (replaces
   ``rope_split`` + SDPA), and :func:`rope_split` itself;
 - :func:`linear` / :func:`linear_rope` / :func:`accumulate`: the projections
@@ -27,6 +29,7 @@ from .kernels import (  # noqa: F401
     cudnn_attention_available,
     encoder_attention,
     flexrel_attention,
+    flexrel_attention_qr,
     flexrel_attention_split,
     linear,
     linear_rope,

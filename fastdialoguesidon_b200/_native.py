@@ -48,6 +48,7 @@ EXPORTED_SYMBOLS = (
     "fds_attn_workspace_bytes",
     "fds_attn_schedule",
     "fds_linear_fwd",
+    "fds_flexrel_qr_attn_fwd",
 )
 
 
@@ -98,6 +99,31 @@ class FdsRopeArgs(ctypes.Structure):
         ("grid_ctas", ctypes.c_int32),
         ("status_host", ctypes.c_void_p),
         ("qk_rotated", ctypes.c_int32),
+    ]
+
+
+class FdsFlexRelQrArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("qr", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("kv_len", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
+        ("status_host", ctypes.c_void_p),
+        ("batch", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("seq_len", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("heads_last", ctypes.c_int32),
+        ("scale", ctypes.c_float),
+        ("timeout_ns", ctypes.c_int64),
+        ("debug_flags", ctypes.c_int32),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_int64),
+        ("grid_ctas", ctypes.c_int32),
     ]
 
 
@@ -154,6 +180,8 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
         lib.fds_rope_attn_fwd.restype = ctypes.c_int
         lib.fds_rope_attn_fwd_static.argtypes = [ctypes.POINTER(FdsRopeArgs), ctypes.c_void_p]
         lib.fds_rope_attn_fwd_static.restype = ctypes.c_int
+        lib.fds_flexrel_qr_attn_fwd.argtypes = [ctypes.POINTER(FdsFlexRelQrArgs), ctypes.c_void_p]
+        lib.fds_flexrel_qr_attn_fwd.restype = ctypes.c_int
         lib.fds_linear_fwd.argtypes = [ctypes.POINTER(FdsLinearArgs), ctypes.c_void_p]
         lib.fds_linear_fwd.restype = ctypes.c_int
         lib.fds_rope_split.argtypes = [

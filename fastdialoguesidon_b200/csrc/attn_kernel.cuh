@@ -190,7 +190,18 @@ struct AttnParams {
     int32_t pieces;           // CTAs [whole_ctas, whole_ctas + pieces) hold the cut last wave (0: none)
     float* parts;             // pieces: [pieces][kMaxItems] slots of 256 rows x kPartRowFloats
     uint32_t* counts;         // pieces: [units - whole_ctas][kSoftmaxWarps] parts counted in
+    // relative bias given as q.rel^T rows in global memory (the TensorRT
+    // plugin's layout: [batch, seq_len, heads, 73], or [batch, heads, seq_len, 73]
+    // with heads_in_z) instead of the in-kernel Q.rel^T product; or null
+    const void* qr;
+    // q / k / v / out laid out [batch, heads, seq_len, 64]: the map's third
+    // coordinate is batch * heads + head and the head's column offset is 0
+    int32_t heads_in_z;
 };
+
+// Tensor-map coordinates of head h of window b: {column of head 0 + x, row, z}.
+__device__ __forceinline__ int head_x(const AttnParams& p, int h) { return p.heads_in_z ? 0 : h * 64; }
+__device__ __forceinline__ int head_z(const AttnParams& p, int b, int h) { return p.heads_in_z ? b * p.heads + h : b; }
 
 template <typename T>
 struct DTypeTraits;
@@ -201,6 +212,7 @@ struct DTypeTraits<__half> {
         __half2 v = __floats2half2_rn(lo, hi);
         return *reinterpret_cast<uint32_t*>(&v);
     }
+    __device__ static __forceinline__ float load_f32(const __half* x) { return __half2float(__ldg(x)); }
 };
 template <>
 struct DTypeTraits<__nv_bfloat16> {
@@ -209,6 +221,7 @@ struct DTypeTraits<__nv_bfloat16> {
         __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
         return *reinterpret_cast<uint32_t*>(&v);
     }
+    __device__ static __forceinline__ float load_f32(const __nv_bfloat16* x) { return __bfloat162float(__ldg(x)); }
 };
 
 // ---------------------------------------------------------------- work items
@@ -493,7 +506,8 @@ struct TileMma {
 // second query tile still takes part in the count-2 barriers of tile 1 (Q and
 // stage releases), after seeing each copy land so that it cannot run ahead.
 template <typename T, bool kRelBias>
-__device__ __forceinline__ void mma_role(uint32_t sbase, uint32_t tmem, WaitCtl ctl, int w, int n_items) {
+__device__ __forceinline__ void mma_role(uint32_t sbase, uint32_t tmem, WaitCtl ctl, int w, int n_items,
+                                         bool qr_mma) {
     const TileMma<T, kRelBias> mma{sbase, tmem, w};
     constexpr int err = FDS_STATUS_TIMEOUT_MMA;
     uint32_t nw = 0;   // S-column writes (QR or S) so far; write k > 0 first waits for read k - 1
@@ -531,7 +545,7 @@ __device__ __forceinline__ void mma_role(uint32_t sbase, uint32_t tmem, WaitCtl 
             continue;
         }
         tc_fence_after();
-        if constexpr (kRelBias) {
+        if (kRelBias && qr_mma) {
             if (!s_free_wait()) break;  // the previous item's last S read out
             tc_fence_after();
             mma.qr();
@@ -837,7 +851,7 @@ __device__ __forceinline__ void finish_part(const AttnParams& p, const float (&o
     if (lane == 0) *count = 0;
 }
 
-template <typename T, bool kRelBias>
+template <typename T, bool kRelBias, bool kQrGlobal>
 __device__ __forceinline__ void softmax_role(uint32_t sbase, uint32_t tmem, const AttnParams& p, WaitCtl ctl,
                                              int warp, int lane, int n_items) {
     const int wg = (warp - kSoftmaxWarp0) >> 2;  // query tile of this warpgroup
@@ -871,8 +885,10 @@ __device__ __forceinline__ void softmax_role(uint32_t sbase, uint32_t tmem, cons
         const Item it = load_item(sbase, idx);
         if (wg == 1 && !it.has_q1) continue;  // this unit has no second query tile
         const int i = it.q_base + wg * kBlockM + row;  // query index in the window
-        T* out_row =
-            reinterpret_cast<T*>(p.out) + (static_cast<int64_t>(it.b) * L + i) * p.out_stride + it.h * kHeadDim;
+        T* out_row = reinterpret_cast<T*>(p.out) +
+                     (p.heads_in_z ? (static_cast<int64_t>(it.b) * p.heads + it.h) * L + i
+                                   : static_cast<int64_t>(it.b) * L + i) * p.out_stride +
+                     head_x(p, it.h);
         if (it.t_end <= it.t_begin) {  // no valid key: the context row is defined as zero
             if (i < L) {
                 const uint4 z = make_uint4(0, 0, 0, 0);
@@ -888,7 +904,24 @@ __device__ __forceinline__ void softmax_role(uint32_t sbase, uint32_t tmem, cons
         rs.l_run = 0.f;
 
         float qr_left = 0.f, qr_right = 0.f;
-        if constexpr (kRelBias) {
+        if constexpr (kRelBias && kQrGlobal) {
+            // this row's 73 relative-key projections from global memory (rows
+            // past the window read as zero, like the Q rows the copies fill)
+            const T* src = static_cast<const T*>(p.qr) +
+                           (p.heads_in_z ? (static_cast<int64_t>(it.b) * p.heads + it.h) * L + i
+                                         : (static_cast<int64_t>(it.b) * L + i) * p.heads + it.h) * kNumPos;
+            const bool in = i < L;
+            const auto qr_at = [&](int r) { return in ? DTypeTraits<T>::load_f32(src + r) * sl : 0.f; };
+            qr_left = qr_at(0);
+            qr_right = qr_at(kNumPos - 1);
+            const uint32_t t = qrow + 4u * (4 + (i & 3));
+#pragma unroll
+            for (int m = 0; m < 7; ++m) st_shared_f32(qrow + 4u * m, qr_left);
+#pragma unroll
+            for (int m = kQrStride - 8; m < kQrStride; ++m) st_shared_f32(qrow + 4u * m, qr_right);
+#pragma unroll 8
+            for (int c = 0; c < kNumPos; ++c) st_shared_f32(t + 4u * c, qr_at(c));
+        } else if constexpr (kRelBias) {
             ok = warp_wait(rs.s_full, rs.s_parity, ctl, err);
             rs.s_parity ^= 1;
             if (!ok) break;
@@ -963,7 +996,7 @@ __device__ __forceinline__ void softmax_role(uint32_t sbase, uint32_t tmem, cons
 
 // ---------------------------------------------------------------- TMA producer
 
-template <bool kRelBias>
+template <bool kRelBias, bool kQrGlobal>
 __device__ __forceinline__ void load_role(uint32_t sbase, const CUtensorMap* map_q, const CUtensorMap* map_k,
                                           const CUtensorMap* map_v, const CUtensorMap* map_r, const AttnParams& p,
                                           WaitCtl ctl, int n_items) {
@@ -979,17 +1012,19 @@ __device__ __forceinline__ void load_role(uint32_t sbase, const CUtensorMap* map
             ok = warp_wait(bar(Smem::kQEmpty), (qi - 1) & 1, ctl, FDS_STATUS_TIMEOUT_LOAD);
             if (!ok) break;
         }
+        const int z = head_z(p, it.b, it.h);
         if (elect_one()) {
-            const uint32_t q_bytes = (it.has_q1 ? 2 : 1) * kTileBytes + ((kRelBias && qi == 0) ? kRelRows * 128 : 0);
-            const int qx = p.q_x0 + it.h * kHeadDim;
+            const bool rel = kRelBias && !kQrGlobal && qi == 0;  // the table for the Q.rel^T MMA
+            const uint32_t q_bytes = (it.has_q1 ? 2 : 1) * kTileBytes + (rel ? kRelRows * 128 : 0);
+            const int qx = p.q_x0 + head_x(p, it.h);
             mbar_arrive_expect_tx(bar(Smem::kQ), q_bytes);
-            tma_load_3d(sbase + Smem::q0, map_q, bar(Smem::kQ), qx, it.q_base, it.b);
-            if (it.has_q1) tma_load_3d(sbase + Smem::q1, map_q, bar(Smem::kQ), qx, it.q_base + kBlockM, it.b);
-            if (kRelBias && qi == 0) tma_load_2d(sbase + Smem::rel, map_r, bar(Smem::kQ), 0, 0);
+            tma_load_3d(sbase + Smem::q0, map_q, bar(Smem::kQ), qx, it.q_base, z);
+            if (it.has_q1) tma_load_3d(sbase + Smem::q1, map_q, bar(Smem::kQ), qx, it.q_base + kBlockM, z);
+            if (rel) tma_load_2d(sbase + Smem::rel, map_r, bar(Smem::kQ), 0, 0);
         }
         __syncwarp();
         ++qi;
-        const int kx = p.k_x0 + it.h * kHeadDim, vx = p.v_x0 + it.h * kHeadDim;
+        const int kx = p.k_x0 + head_x(p, it.h), vx = p.v_x0 + head_x(p, it.h);
         for (int j = it.t_begin; j < it.t_end; ++j) {
             const int st = g % kStages;
             const uint32_t par = ((g / kStages) - 1) & 1;
@@ -999,7 +1034,7 @@ __device__ __forceinline__ void load_role(uint32_t sbase, const CUtensorMap* map
             }
             if (elect_one()) {
                 mbar_arrive_expect_tx(bar(Smem::kKFull + st), kTileBytes);
-                tma_load_3d(sbase + Smem::k + st * kTileBytes, map_k, bar(Smem::kKFull + st), kx, j * kBlockN, it.b);
+                tma_load_3d(sbase + Smem::k + st * kTileBytes, map_k, bar(Smem::kKFull + st), kx, j * kBlockN, z);
             }
             __syncwarp();
             if (g >= kStages) {
@@ -1011,7 +1046,7 @@ __device__ __forceinline__ void load_role(uint32_t sbase, const CUtensorMap* map
             }
             if (elect_one()) {
                 mbar_arrive_expect_tx(bar(Smem::kVFull + st), kTileBytes);
-                tma_load_3d(sbase + Smem::v + st * kTileBytes, map_v, bar(Smem::kVFull + st), vx, j * kBlockN, it.b);
+                tma_load_3d(sbase + Smem::v + st * kTileBytes, map_v, bar(Smem::kVFull + st), vx, j * kBlockN, z);
             }
             __syncwarp();
             ++g;
@@ -1034,7 +1069,9 @@ __device__ __forceinline__ void load_role(uint32_t sbase, const CUtensorMap* map
 
 // ---------------------------------------------------------------- kernel
 
-template <typename T, bool kRelBias>
+// kQrGlobal (with kRelBias): the relative-key projections come from global
+// memory (p.qr, the TensorRT plugin's form) instead of the Q.rel^T MMA.
+template <typename T, bool kRelBias, bool kQrGlobal = false>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                     const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_r,
@@ -1087,7 +1124,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tensormap(&map_q);
         prefetch_tensormap(&map_k);
         prefetch_tensormap(&map_v);
-        if (kRelBias) prefetch_tensormap(&map_r);
+        if (kRelBias && !kQrGlobal) prefetch_tensormap(&map_r);
     }
     if (warp == kTmemWarp) {
         tmem_alloc(tmem_holder, kTmemCols);
@@ -1105,7 +1142,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // exactly once, so all roles have finished with TMEM when it opens).
     if (warp >= kSoftmaxWarp0) {
         setmaxnreg_inc<RegSplit<kRelBias>::kSoftmax>();
-        softmax_role<T, kRelBias>(sbase, tmem, p, ctl, warp, lane, n_items);
+        softmax_role<T, kRelBias, kQrGlobal>(sbase, tmem, p, ctl, warp, lane, n_items);
         __syncwarp();
         tc_fence_before();
         named_barrier_sync(1, kThreads);
@@ -1117,9 +1154,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool go = true;
             if (p.debug_flags & FDS_DEBUG_FORCE_TIMEOUT)
                 go = warp_wait(sbase + Smem::bars + 8u * Smem::kNever, 0, ctl, FDS_STATUS_TIMEOUT_MMA);
-            if (go) mma_role<T, kRelBias>(sbase, tmem, ctl, (warp - kMmaWarp0) >> 1, n_items);
+            if (go) mma_role<T, kRelBias>(sbase, tmem, ctl, (warp - kMmaWarp0) >> 1, n_items, !kQrGlobal);
         } else if (warp == kLoadWarp) {
-            load_role<kRelBias>(sbase, &map_q, &map_k, &map_v, &map_r, p, ctl, n_items);
+            load_role<kRelBias, kQrGlobal>(sbase, &map_q, &map_k, &map_v, &map_r, p, ctl, n_items);
         }
         __syncwarp();
         tc_fence_before();

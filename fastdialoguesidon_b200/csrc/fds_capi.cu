@@ -237,10 +237,10 @@ Plan plan_schedule(int64_t batch, int64_t heads, int64_t seq_len, bool has_kv_le
 }
 
 // Launches on `plan`; the workspace is split into counts and slots.
-template <typename T, bool kRelBias>
+template <typename T, bool kRelBias, bool kQrGlobal = false>
 int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mr,
                 fds::AttnParams p, int batch, const Workspace& ws, cudaStream_t stream) {
-    auto kern = fds::attn_fwd_kernel<T, kRelBias>;
+    auto kern = fds::attn_fwd_kernel<T, kRelBias, kQrGlobal>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fds::Smem::alloc);
     if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     p.row_blocks = (p.seq_len + fds::kRowsPerCta - 1) / fds::kRowsPerCta;
@@ -422,6 +422,62 @@ int fds_flexrel_attn_fwd(const FdsFlexRelArgs* a, void* stream) {
     const Workspace ws{a->workspace, a->workspace_bytes, a->grid_ctas};
     rc = a->dtype == FDS_DTYPE_FP16 ? launch_attn<__half, true>(mqkv, mqkv, mqkv, mrel, p, a->batch, ws, s)
                                     : launch_attn<__nv_bfloat16, true>(mqkv, mqkv, mqkv, mrel, p, a->batch, ws, s);
+    return rc == FDS_OK ? ok() : rc;
+}
+
+int fds_flexrel_qr_attn_fwd(const FdsFlexRelQrArgs* a, void* stream) {
+    if (a == nullptr) return fail(FDS_ERR_INVALID_ARGUMENT, "null args");
+    if (a->q == nullptr || a->k == nullptr || a->v == nullptr || a->qr == nullptr || a->out == nullptr)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "null q/k/v/qr/out pointer");
+    if (a->head_dim != 64) return fail(FDS_ERR_INVALID_ARGUMENT, "head_dim must be 64 (got %d)", a->head_dim);
+    if (a->dtype != FDS_DTYPE_FP16 && a->dtype != FDS_DTYPE_BF16)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "dtype must be FDS_DTYPE_FP16 or FDS_DTYPE_BF16 (got %d)", a->dtype);
+    if (a->batch < 1 || a->heads < 1 || a->seq_len < 1)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "batch, heads and seq_len must be >= 1 (got %d, %d, %d)", a->batch,
+                    a->heads, a->seq_len);
+    if (static_cast<int64_t>(a->batch) * a->heads > 65535)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "batch * heads must be <= 65535");
+    if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->out))
+        return fail(FDS_ERR_INVALID_ARGUMENT, "q, k, v and out must be 16-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(a->qr) & 1u) != 0)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "qr must be 2-byte aligned");
+    if (!(a->scale > 0.f)) return fail(FDS_ERR_INVALID_ARGUMENT, "scale must be > 0");
+    int rc = check_device();
+    if (rc != FDS_OK) return rc;
+
+    const int64_t hid = static_cast<int64_t>(a->heads) * 64;
+    CUtensorMap mq, mk, mv;
+    if (a->heads_last) {
+        // rows (b, t) of heads * 64 columns
+        if ((rc = make_rows_map(&mq, a->q, a->dtype, hid, a->seq_len, a->batch, hid, fds::kBlockM)) != FDS_OK) return rc;
+        if ((rc = make_rows_map(&mk, a->k, a->dtype, hid, a->seq_len, a->batch, hid, fds::kBlockM)) != FDS_OK) return rc;
+        if ((rc = make_rows_map(&mv, a->v, a->dtype, hid, a->seq_len, a->batch, hid, fds::kBlockM)) != FDS_OK) return rc;
+    } else {
+        // rows t of 64 columns per (b, h): the map's third coordinate is b * heads + h
+        const int64_t bh = static_cast<int64_t>(a->batch) * a->heads;
+        if ((rc = make_rows_map(&mq, a->q, a->dtype, 64, a->seq_len, bh, 64, fds::kBlockM)) != FDS_OK) return rc;
+        if ((rc = make_rows_map(&mk, a->k, a->dtype, 64, a->seq_len, bh, 64, fds::kBlockM)) != FDS_OK) return rc;
+        if ((rc = make_rows_map(&mv, a->v, a->dtype, 64, a->seq_len, bh, 64, fds::kBlockM)) != FDS_OK) return rc;
+    }
+    fds::AttnParams p{};
+    p.out = a->out;
+    p.out_stride = a->heads_last ? hid : 64;
+    p.kv_len = a->kv_len;
+    p.status = a->status;
+    p.status_host = a->status_host;
+    p.timeout_ns = a->timeout_ns;
+    p.heads = a->heads;
+    p.seq_len = a->seq_len;
+    p.q_x0 = p.k_x0 = p.v_x0 = 0;
+    p.scale_log2 = a->scale * 1.4426950408889634f;
+    p.debug_flags = a->debug_flags;
+    p.qr = a->qr;
+    p.heads_in_z = a->heads_last ? 0 : 1;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const Workspace ws{a->workspace, a->workspace_bytes, a->grid_ctas};
+    // map_r is not read when qr comes from global memory
+    rc = a->dtype == FDS_DTYPE_FP16 ? launch_attn<__half, true, true>(mq, mk, mv, mq, p, a->batch, ws, s)
+                                    : launch_attn<__nv_bfloat16, true, true>(mq, mk, mv, mq, p, a->batch, ws, s);
     return rc == FDS_OK ? ok() : rc;
 }
 

@@ -252,6 +252,59 @@ def flexrel_attention(qkv: torch.Tensor, batch: int, heads: int, rel: torch.Tens
     return out
 
 
+def flexrel_attention_qr(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, qr: torch.Tensor,
+                         out: torch.Tensor | None = None, heads_last: bool = True,
+                         kv_len: torch.Tensor | None = None, *, timeout_ns: int = 0, debug_flags: int = 0,
+                         balanced: bool = True, grid_ctas: int = 0) -> torch.Tensor:
+    """Relative-key attention with the bias projections given: the TensorRT
+    plugin's form (sidon::FlexRelAttnQR / QRD). q, k, v, out [B, L, H, 64]
+    (``heads_last``) or [B, H, L, 64], qr = q . rel^T [B, L, H, 73] or
+    [B, H, L, 73], all contiguous fp16 / bf16;
+    S = (q k^T + qr[.., clamp(j - i, -64, 8) + 64]) / 8, softmax, V.
+    Reference: ``flexrel_attention_qr`` (trt/src/fastdialoguesidon/
+    flexrel_triton.py:749-780). ``kv_len`` as in :func:`flexrel_attention`."""
+    for name, t in (("q", q), ("k", k), ("v", v), ("qr", qr)):
+        _check(isinstance(t, torch.Tensor) and t.dim() == 4 and t.is_contiguous(),
+               f"{name} must be a contiguous 4-D tensor")
+        _check(t.dtype in _DTYPES and t.dtype == q.dtype and t.device == q.device,
+               f"{name} must be float16 / bfloat16 like q, on q's device")
+    _check(q.shape == k.shape == v.shape, "q, k and v must have the same shape")
+    if heads_last:
+        batch, length, heads, dim = q.shape
+        _check(qr.shape == (batch, length, heads, NUM_POS), f"qr must be [{batch}, {length}, {heads}, {NUM_POS}]")
+    else:
+        batch, heads, length, dim = q.shape
+        _check(qr.shape == (batch, heads, length, NUM_POS), f"qr must be [{batch}, {heads}, {length}, {NUM_POS}]")
+    _check(dim == HEAD_DIM, f"head_dim must be 64, got {dim}")
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _check(t.data_ptr() % 16 == 0, f"{name} must be 16-byte aligned")
+    if out is None:
+        out = torch.empty_like(q)
+    else:
+        _check(out.shape == q.shape and out.dtype == q.dtype and out.device == q.device and out.is_contiguous()
+               and out.data_ptr() % 16 == 0, f"out must be a contiguous {tuple(q.shape)} {q.dtype} tensor")
+    kv_ptr = None
+    if kv_len is not None:
+        _check(isinstance(kv_len, torch.Tensor) and kv_len.dtype == torch.int32
+               and kv_len.shape == (batch,) and kv_len.is_contiguous() and kv_len.device == q.device,
+               f"kv_len must be a contiguous int32 CUDA tensor of shape [{batch}] on q's device")
+        kv_ptr = kv_len.data_ptr()
+    _on_cuda(q, k, v, qr, out)
+    dev = q.device
+    _raise_if_timed_out(dev)
+    lib = N.load()
+    with torch.cuda.device(dev):
+        args = N.FdsFlexRelQrArgs(
+            q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), qr=qr.data_ptr(), out=out.data_ptr(),
+            kv_len=kv_ptr, status=_status(dev).data_ptr(), status_host=_status_mirror(dev).data_ptr(),
+            batch=batch, heads=heads, seq_len=length, head_dim=dim, dtype=_DTYPES[q.dtype],
+            heads_last=1 if heads_last else 0, scale=1.0 / math.sqrt(dim), timeout_ns=int(timeout_ns),
+            debug_flags=int(debug_flags), **_schedule(dev, lib, balanced and kv_len is None, grid_ctas))
+        rc = lib.fds_flexrel_qr_attn_fwd(ctypes.byref(args), _stream_ptr(dev))
+    _raise_rc(rc, "fds_flexrel_qr_attn_fwd")
+    return out
+
+
 def flexrel_attention_split(qkv: torch.Tensor, batch: int, heads: int, rel: torch.Tensor,
                             out: torch.Tensor | None = None) -> torch.Tensor:
     """Same contract and result as :func:`flexrel_attention`

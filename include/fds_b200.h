@@ -110,6 +110,44 @@ typedef struct FdsFlexRelArgs {
 FDS_API int fds_flexrel_attn_fwd(const FdsFlexRelArgs* args, void* stream);
 
 /*
+ * The same relative_key attention in the TensorRT plugin's form: separate q, k,
+ * v and the relative-key projections qr = q . rel^T (unscaled, as the graph's
+ * MatMul produces them) as inputs, so the bias is read, not computed:
+ *   S[b,h,i,j] = (q_i . k_j + qr[b,i,h,clamp(j - i, -64, +8) + 64]) * scale
+ * Layouts (contiguous): heads_last = 1: q, k, v, out [batch, seq_len, heads, 64]
+ * and qr [batch, seq_len, heads, 73] (the plugin's); heads_last = 0: [batch,
+ * heads, seq_len, 64] and [batch, heads, seq_len, 73]. kv_len, scale, status,
+ * timeout and workspace as in FdsFlexRelArgs.
+ * Replaces: trt/src/fastdialoguesidon/flexrel_triton.py:749 flexrel_attention_qr
+ * and the sidon::FlexRelAttnQR / FlexRelAttnQRD plugins (:902-1028), whose
+ * kernel body is _flexrel_qr_body (:559).
+ */
+typedef struct FdsFlexRelQrArgs {
+    const void* q;            /* device, dtype, see the layouts above */
+    const void* k;
+    const void* v;
+    const void* qr;           /* device, dtype, [.., 73] */
+    void* out;                /* device, dtype, q's layout */
+    const int32_t* kv_len;    /* device [batch], or NULL */
+    int32_t* status;          /* device word for bounded-wait errors, or NULL */
+    int32_t* status_host;     /* mapped pinned host mirror, or NULL */
+    int32_t batch;
+    int32_t heads;
+    int32_t seq_len;
+    int32_t head_dim;         /* must be 64 */
+    int32_t dtype;            /* FDS_DTYPE_* */
+    int32_t heads_last;       /* 1: [batch, seq_len, heads, ..]; 0: [batch, heads, seq_len, ..] */
+    float scale;              /* the plugin uses 1/sqrt(64) */
+    int64_t timeout_ns;
+    int32_t debug_flags;
+    void* workspace;          /* as in FdsFlexRelArgs */
+    int64_t workspace_bytes;
+    int32_t grid_ctas;
+} FdsFlexRelQrArgs;
+
+FDS_API int fds_flexrel_qr_attn_fwd(const FdsFlexRelQrArgs* args, void* stream);
+
+/*
  * DiT head RoPE self-attention (bidirectional, no bias, no mask):
  *   q' = q*cos[t] + rotate_half(q)*sin[t], k' likewise (rotate_half(x) = [-x2, x1]),
  *   O = softmax(q' k'^T * scale) V

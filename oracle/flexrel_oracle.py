@@ -67,6 +67,36 @@ def flexrel_core(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rel: torch.T
     return out
 
 
+def flexrel_core_qr(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, qr: torch.Tensor,
+                    kv_len=None, chunk: int = 512) -> torch.Tensor:
+    """Relative-key attention with the projections qr = q . rel^T given (the
+    TensorRT plugin's form): q, k, v [B, H, L, D], qr [B, H, L, 73] -> [B, H, L, D]
+    fp32, S = (q.k^T + qr[.., clamp(j - i, -64, 8) + 64]) / sqrt(D), softmax,
+    times V. Restates _flexrel_qr_body (trt/src/fastdialoguesidon/
+    flexrel_triton.py:559-700: qr_left / qr_right outside the band, the gathered
+    qr inside it, all scaled like q.k). ``kv_len`` as in :func:`flexrel_core`."""
+    q, k, v, qr = (t.float() for t in (q, k, v, qr))
+    batch, heads, length, dim = q.shape
+    scale = 1.0 / math.sqrt(dim)
+    out = torch.empty(batch, heads, length, dim, dtype=torch.float32)
+    kmask = None
+    if kv_len is not None:
+        kv = torch.as_tensor(kv_len).to(torch.int64).clamp(0, length)
+        kmask = torch.arange(length)[None, :] >= kv[:, None]
+    for start in range(0, length, chunk):
+        stop = min(start + chunk, length)
+        idx = rel_index(length, start, stop)
+        bias = torch.gather(qr[:, :, start:stop], 3, idx.view(1, 1, stop - start, length).expand(batch, heads, -1, -1))
+        scores = (q[:, :, start:stop] @ k.transpose(-2, -1) + bias) * scale
+        if kmask is not None:
+            scores = scores.masked_fill(kmask[:, None, None, :], float("-inf"))
+        p = torch.softmax(scores, dim=-1)
+        if kmask is not None:
+            p = torch.nan_to_num(p, nan=0.0)
+        out[:, :, start:stop] = p @ v
+    return out
+
+
 def flexrel_rows(q, k, v, rel, start: int, stop: int) -> torch.Tensor:
     """Rows [start, stop) of :func:`flexrel_core` (no mask): one chunk of
     torch_core_chunked (flexrel_triton.py:312-328). Used to time the CPU path."""

@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol():
 def test_struct_layouts_match_header():
     text = HEADER.read_text()
     for struct, cls in (("FdsFlexRelArgs", N.FdsFlexRelArgs), ("FdsRopeArgs", N.FdsRopeArgs),
-                        ("FdsLinearArgs", N.FdsLinearArgs)):
+                        ("FdsLinearArgs", N.FdsLinearArgs), ("FdsFlexRelQrArgs", N.FdsFlexRelQrArgs)):
         body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (struct, struct), text, re.S).group(1)
         fields = re.findall(r"^\s*[\w\s\*]+?\b(\w+);", body, re.M)
         assert fields == [f[0] for f in cls._fields_], (struct, fields)
@@ -95,6 +95,24 @@ def test_c_abi_linear_rejects_invalid_arguments_before_launch(bad):
     assert rc == N.FDS_ERR_INVALID_ARGUMENT, bad
     assert lib.fds_last_error()
     assert lib.fds_linear_fwd(None, None) == N.FDS_ERR_INVALID_ARGUMENT
+
+
+def _qr_args(**kw):
+    base = dict(q=16, k=16, v=16, qr=16, out=16, kv_len=None, status=None, status_host=None, batch=1, heads=16,
+                seq_len=100, head_dim=64, dtype=N.FDS_DTYPE_FP16, heads_last=1, scale=0.125, timeout_ns=0,
+                debug_flags=0)
+    base.update(kw)
+    return N.FdsFlexRelQrArgs(**base)
+
+
+@pytest.mark.parametrize("bad", [
+    dict(head_dim=32), dict(dtype=4), dict(batch=0), dict(seq_len=0), dict(q=0), dict(qr=0), dict(k=24),
+    dict(qr=17), dict(scale=-1.0), dict(batch=5000),
+])
+def test_c_abi_qr_rejects_invalid_arguments_before_launch(bad):
+    lib = N.load()
+    assert lib.fds_flexrel_qr_attn_fwd(ctypes.byref(_qr_args(**bad)), None) == N.FDS_ERR_INVALID_ARGUMENT
+    assert lib.fds_last_error()
 
 
 def test_linear_validation():

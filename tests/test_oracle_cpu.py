@@ -140,3 +140,16 @@ def test_exp2_polynomial_error_bound():
     assert np.all(below >= 0) and np.all(below <= 2.0 ** -124), below
     above = exp2_poly(np.array([66.4, 67, 100, 1e6, 3e38, np.inf], dtype=np.float32))
     assert np.all(np.isfinite(above)) and np.all(above >= 2.0 ** 65), above
+
+
+def test_qr_form_matches_the_core():
+    """flexrel_core_qr (the plugin form, qr given) equals flexrel_core when qr
+    is q.rel^T in fp32: the QR-form oracle rests on the golden-pinned core."""
+    gen = torch.Generator().manual_seed(12)
+    q, k, v = (torch.randn(2, 3, 150, 64, generator=gen) for _ in range(3))
+    rel = torch.randn(73, 64, generator=gen) * 0.3
+    qr = torch.einsum("bhld,rd->bhlr", q, rel)
+    for kv in (None, [150, 77]):
+        a = O.flexrel_core(q, k, v, rel, kv_len=kv)
+        b = O.flexrel_core_qr(q, k, v, qr, kv_len=kv)
+        assert O.max_abs(a, b) < 1e-5
