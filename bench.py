@@ -648,18 +648,30 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         dper: list[float] = []
         dms = time_graph(dit_step, dsteps, args.warmup, device, dist_on, per_step=dper)
         F.check_status(device)
-        dit = (dms, dsteps, statistics.median(dper))
+        # the same 8 layers when the QKV projection's epilogue has applied RoPE
+        # (linear_rope): the attention reads q | k rotated, no RoPE pass
+        drot = [F.rope_split(q, L_WINDOW, DIT_HEADS, cos, sin) for q in dq]
+        drot = [torch.cat([r[0], r[1], r[2]], 1).contiguous() for r in drot]
+
+        def dit_rot_step():
+            for q, o in zip(drot, dout):
+                F.rotated_attention(q, 1, DIT_HEADS, out=o, balanced=bal)
+
+        rms = time_graph(dit_rot_step, dsteps, args.warmup, device, dist_on)
+        F.check_status(device)
+        del drot
+        dit = (dms, dsteps, statistics.median(dper), rms)
         dit_inputs = (dq, cos, sin, dout)
 
     c3 = None if args.no_config3 else config3_leg(args, rank, device, dist_on, bal)
     tp = None if args.no_throughput else throughput_leg(args, rank, world, device, dist_on, bal)
 
     vals = [ms, e2e_ms, copy["h2d_ms"], copy["d2h_ms"], copy["both_ms"], dit[0] if dit else 0.0,
-            c3["ms"] if c3 else 0.0, tp["ms"] if tp else 0.0]
+            c3["ms"] if c3 else 0.0, tp["ms"] if tp else 0.0, dit[3] if dit else 0.0]
     t = torch.tensor(vals, dtype=torch.float64, device=device)
     if dist_on:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms, e2e_ms, h2d_ms, d2h_ms, both_ms, dms, c3_ms, tp_ms = (float(x) for x in t.tolist())
+    ms, e2e_ms, h2d_ms, d2h_ms, both_ms, dms, c3_ms, tp_ms, rms = (float(x) for x in t.tolist())
 
     if rank == 0:
         K = args.steps
@@ -705,7 +717,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                            "ms_per_window": round(dms / dsteps, 4), "median_ms_per_window": round(dit[2], 4),
                            "tflops": round(FLOP_DIT_LAYER / (dper_ms * 1e-3) / 1e12, 1),
                            "frac": round(FLOP_DIT_LAYER / (dper_ms * 1e-3) / 1e12 / peak, 4),
-                           "steps": dsteps, "launches_per_window": 2 * DIT_LAYERS}
+                           "steps": dsteps, "launches_per_window": 2 * DIT_LAYERS,
+                           "rotated_ms_per_window": round(rms / dsteps, 4),
+                           "rotated_note": "q | k rotated by the QKV projection's epilogue (linear_rope): "
+                                           "8 attention launches, no RoPE pass"}
         if c3:
             per_batch = c3_ms / c3["steps"]
             line["config3"] = {

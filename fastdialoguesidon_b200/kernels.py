@@ -76,7 +76,10 @@ def _status(device: torch.device) -> torch.Tensor:
     idx = _dev_index(device)
     st = _status_words.get(idx)
     if st is None:
-        st = torch.zeros(4, dtype=torch.int32, device=torch.device("cuda", idx))
+        # library state outlives the caller's context: never an inference tensor
+        # (the reference pipeline runs under torch.inference_mode)
+        with torch.inference_mode(False):
+            st = torch.zeros(4, dtype=torch.int32, device=torch.device("cuda", idx))
         _status_words[idx] = st
     return st
 
@@ -87,7 +90,8 @@ def _status_mirror(device: torch.device) -> torch.Tensor:
     idx = _dev_index(device)
     m = _status_mirrors.get(idx)
     if m is None:
-        m = torch.zeros(4, dtype=torch.int32).pin_memory()
+        with torch.inference_mode(False):
+            m = torch.zeros(4, dtype=torch.int32).pin_memory()
         _status_mirrors[idx] = m
     return m
 
@@ -113,13 +117,14 @@ def check_status(device: torch.device | int | None = None, clear: bool = True) -
     torch.cuda.synchronize(dev)
     bits = int(st[0].item()) | int(mirror[0])
     if clear and bits:
-        st.zero_()
-        mirror.zero_()
-        for (idx, _), ws in _workspaces.items():
-            if idx == dev.index:
-                ws.zero_()  # an aborted split may leave part counts behind
-        for ws in _spare_workspaces.get(dev.index, []):
-            ws.zero_()
+        with torch.inference_mode(False):
+            st.zero_()
+            mirror.zero_()
+            for (idx, _), ws in _workspaces.items():
+                if idx == dev.index:
+                    ws.zero_()  # an aborted split may leave part counts behind
+            for ws in _spare_workspaces.get(dev.index, []):
+                ws.zero_()
         torch.cuda.synchronize(dev)
     if bits:
         raise FdsError(f"FDS kernel on {dev} reported a bounded-wait timeout (status bits 0x{bits:x})")
@@ -150,13 +155,14 @@ def _workspace(device: torch.device, lib) -> torch.Tensor | None:
         if nbytes <= 0:
             raise FdsError(f"fds_attn_workspace_bytes failed: {N.last_error()}")
         cuda = torch.device("cuda", idx)
-        ws = torch.zeros(nbytes, dtype=torch.uint8, device=cuda)
-        if idx not in _spare_workspaces:
-            # zero-filled now, handed to the first captures on new streams;
-            # the one-time wait makes the fill complete before any graph runs
-            _spare_workspaces[idx] = [torch.zeros(nbytes, dtype=torch.uint8, device=cuda)
-                                      for _ in range(_SPARE_WORKSPACES)]
-            torch.cuda.current_stream(cuda).synchronize()
+        with torch.inference_mode(False):
+            ws = torch.zeros(nbytes, dtype=torch.uint8, device=cuda)
+            if idx not in _spare_workspaces:
+                # zero-filled now, handed to the first captures on new streams;
+                # the one-time wait makes the fill complete before any graph runs
+                _spare_workspaces[idx] = [torch.zeros(nbytes, dtype=torch.uint8, device=cuda)
+                                          for _ in range(_SPARE_WORKSPACES)]
+                torch.cuda.current_stream(cuda).synchronize()
     _workspaces[key] = ws
     return ws
 

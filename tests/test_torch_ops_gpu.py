@@ -105,3 +105,24 @@ def test_timeout_reaches_the_next_call_without_a_sync(cuda_device):
     out = torch.ops.fds.flexrel_attention(qkv, 1, 2, rel)   # cleared: calls work again
     assert F.check_status() == 0
     assert torch.equal(out, F.flexrel_attention(qkv, 1, 2, rel))
+
+
+def test_state_created_under_inference_mode(cuda_device):
+    """The reference pipeline calls the ops under torch.inference_mode
+    (runtime.py:135); the library's per-device state made there must stay
+    usable outside it (check_status clears it in place)."""
+    import fastdialoguesidon_b200.kernels as K
+
+    qkv, rel = _inputs(1, 300, 2, seed=13, device=cuda_device)
+    saved = dict(K._status_words), dict(K._status_mirrors)
+    K._status_words.clear()
+    K._status_mirrors.clear()
+    try:
+        with torch.inference_mode():
+            F.flexrel_attention(qkv, 1, 2, rel, timeout_ns=2_000_000, debug_flags=N.FDS_DEBUG_FORCE_TIMEOUT)
+        with pytest.raises(F.FdsError, match="timeout"):
+            F.check_status()
+        assert F.check_status() == 0
+    finally:
+        K._status_words.update(saved[0])
+        K._status_mirrors.update(saved[1])
