@@ -73,8 +73,9 @@ def parse_args():
     ap.add_argument("--schedule", choices=("auto", "unit"), default="auto",
                     help="auto: the library picks whole units per CTA or the balanced (stream-K) grid; "
                          "unit: always one 256-row unit per CTA")
-    ap.add_argument("--case", choices=("enc1", "dit1"), default=None,
-                    help="profiling case: W + K eager launches of one layer (encoder or DiT) at L=6000")
+    ap.add_argument("--case", choices=("enc1", "dit1", "qkv"), default=None,
+                    help="profiling case: W + K eager launches of one layer's attention (encoder or DiT) or of "
+                         "the encoder's QKV projection (qkv) at L=6000")
     ap.add_argument("--no-config3", action="store_true")
     ap.add_argument("--no-throughput", action="store_true")
     ap.add_argument("--no-linear", action="store_true")
@@ -767,7 +768,13 @@ def run_case(args) -> None:
     device = torch.device("cuda", 0)
     bal = args.schedule == "auto"
     gen = torch.Generator(device=device).manual_seed(7)
-    if args.case == "enc1":
+    if args.case == "qkv":
+        x = torch.randn(L_WINDOW, ENC_HEADS * HEAD_DIM, generator=gen, device=device).half()
+        w = (torch.randn(3 * ENC_HEADS * HEAD_DIM, ENC_HEADS * HEAD_DIM, generator=gen, device=device) * 0.02).half()
+        b = (torch.randn(3 * ENC_HEADS * HEAD_DIM, generator=gen, device=device) * 0.02).half()
+        out = torch.empty(L_WINDOW, 3 * ENC_HEADS * HEAD_DIM, dtype=torch.float16, device=device)
+        fn, flop = (lambda: F.linear(x, w, b, out=out)), 2.0 * L_WINDOW * x.shape[1] * w.shape[0]
+    elif args.case == "enc1":
         qkv = (torch.randn(L_WINDOW, 3 * ENC_HEADS * HEAD_DIM, generator=gen, device=device) * 0.64).half()
         rel = (torch.randn(73, HEAD_DIM, generator=gen, device=device) * 0.02).half()
         out = torch.empty(L_WINDOW, ENC_HEADS * HEAD_DIM, dtype=torch.float16, device=device)
