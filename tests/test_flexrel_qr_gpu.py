@@ -67,3 +67,19 @@ def test_agrees_with_the_fused_qkv_entry_point(cuda_device):
     F.check_status()
     assert O.max_abs(ref.float().cpu(), out.float().cpu()) <= MAX_ABS
     assert O.snr_db(ref.float().cpu(), out.float().cpu()) >= MIN_SNR
+
+
+def test_bf16(cuda_device):
+    """bf16 operands (the plugin accepts BF16|FP16): the reference's own bf16
+    bar, SNR > 40 dB (triton/tests/test_kernels.py:119)."""
+    B, L, H = 1, 700, 8
+    g = torch.Generator().manual_seed(17)
+    q, k, v = ((torch.randn(B, L, H, 64, generator=g) * 0.64).to(torch.bfloat16) for _ in range(3))
+    rel = (torch.randn(73, 64, generator=g) * 0.3).to(torch.bfloat16)
+    qr = torch.einsum("blhd,rd->blhr", q.float(), rel.float()).to(torch.bfloat16)
+    d = cuda_device
+    out = F.flexrel_attention_qr(q.to(d), k.to(d), v.to(d), qr.to(d))
+    F.check_status()
+    t = (lambda x: x.permute(0, 2, 1, 3))
+    exp = O.flexrel_core_qr(t(q), t(k), t(v), t(qr)).permute(0, 2, 1, 3)
+    assert O.snr_db(exp, out.float().cpu()) > 40.0

@@ -176,3 +176,32 @@ def test_dit_attention_layer_with_rope_epilogue(cuda_device):
     for got in (fused, separate):
         err, snr = O.max_abs(exp, got.float().cpu()), O.snr_db(exp, got.float().cpu())
         assert err <= 2e-3 and snr >= 55.0, (err, snr)
+
+
+def test_linear_rope_bf16(cuda_device):
+    B, L, H = 1, 1000, 12
+    hid = H * 64
+    x, w, b, xd, wd, bd = _operands(B * L, hid, 3 * hid, seed=41, dtype=torch.bfloat16)
+    cos, sin = F.rope_tables(L, cuda_device)
+    got = F.linear_rope(xd, wd, bd, cos, sin, L, H).float().cpu()
+    y = _ref(x, w, b).to(torch.bfloat16)
+    exp = O.rope_split(y, L, H, cos.cpu(), sin.cpu())
+    bound = 2 * ULP[torch.bfloat16] * float(exp.abs().max()) + 1e-6
+    for part in range(3):
+        e, g_ = exp[part], got[:, part * hid:(part + 1) * hid]
+        assert O.max_abs(e, g_) <= bound and O.snr_db(e, g_) >= MIN_SNR[torch.bfloat16], part
+    F.check_status()
+
+
+def test_accumulate_bf16_with_bias(cuda_device):
+    m, k, n = 700, 768, 768
+    g = torch.Generator().manual_seed(43)
+    x = torch.randn(m, n, generator=g)
+    a = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    bias = (torch.randn(n, generator=g) * 0.1).to(torch.bfloat16)
+    xd = x.to(cuda_device)
+    F.accumulate(xd, a.to(cuda_device), w.to(cuda_device), bias.to(cuda_device))
+    F.check_status()
+    delta = (a.double() @ w.double().t() + bias.double()).float()
+    assert O.max_abs(x + delta, xd.cpu()) <= 1e-4 * float(delta.abs().max()) + 1e-5
