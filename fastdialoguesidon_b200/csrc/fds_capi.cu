@@ -140,6 +140,26 @@ int make_matrix_map(CUtensorMap* map, const void* base, int dtype, int64_t cols,
     return FDS_OK;
 }
 
+// The linear layers' output for the epilogue's TMA copies: boxes of 32 rows x
+// 128 bytes (64 fp16 / bf16 or 32 fp32 columns), 128-byte swizzle, the layout
+// the epilogue stages each box in.
+int make_out_map(CUtensorMap* map, void* base, bool f32, int dtype, int64_t cols, int64_t rows, int64_t row_stride) {
+    EncodeTiledFn enc = encode_fn();
+    if (enc == nullptr) return fail(FDS_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled unavailable from the driver");
+    const int esize = f32 ? 4 : 2;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride * esize)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esize), 32};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapDataType dt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : dtype == FDS_DTYPE_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                             : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUresult r = enc(map, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(FDS_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled(output) failed (%d)", static_cast<int>(r));
+    return FDS_OK;
+}
+
 // Kernels are launched with programmatic stream serialization: a launch may
 // start its CTAs while the previous kernel in the stream drains, and waits in
 // the kernel (griddepcontrol.wait) before touching memory. FDS_PDL=0 in the
@@ -313,25 +333,25 @@ int fds_detail::set_error(int code, const char* fmt, ...) {
 namespace {
 
 template <typename T, int BN, int kEpi>
-int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const fds::gemm::Params& p, int grid,
-                cudaStream_t stream) {
+int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const fds::gemm::Params& p,
+                int grid, cudaStream_t stream) {
     auto kern = fds::gemm::gemm_kernel<T, BN, kEpi>;
     constexpr int smem = fds::gemm::Smem<BN>::alloc;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "cudaFuncSetAttribute(gemm): %s", cudaGetErrorString(e));
-    e = launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(fds::gemm::kThreads), smem, stream, ma, mb, p);
+    e = launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(fds::gemm::kThreads), smem, stream, ma, mb, mo, p);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "linear launch: %s", cudaGetErrorString(e));
     return FDS_OK;
 }
 
 template <typename T, int BN>
-int launch_gemm_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const fds::gemm::Params& p, int grid,
-                    cudaStream_t stream) {
+int launch_gemm_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo,
+                    const fds::gemm::Params& p, int grid, cudaStream_t stream) {
     switch (epi) {
-        case FDS_EPILOGUE_STORE: return launch_gemm<T, BN, fds::gemm::kStore>(ma, mb, p, grid, stream);
-        case FDS_EPILOGUE_ROPE: return launch_gemm<T, BN, fds::gemm::kRope>(ma, mb, p, grid, stream);
-        default: return launch_gemm<T, BN, fds::gemm::kAccum>(ma, mb, p, grid, stream);
+        case FDS_EPILOGUE_STORE: return launch_gemm<T, BN, fds::gemm::kStore>(ma, mb, mo, p, grid, stream);
+        case FDS_EPILOGUE_ROPE: return launch_gemm<T, BN, fds::gemm::kRope>(ma, mb, mo, p, grid, stream);
+        default: return launch_gemm<T, BN, fds::gemm::kAccum>(ma, mb, mo, p, grid, stream);
     }
 }
 
@@ -595,12 +615,11 @@ int fds_linear_fwd(const FdsLinearArgs* a, void* stream) {
     const int64_t tiles = static_cast<int64_t>((a->m + fds::gemm::kBM - 1) / fds::gemm::kBM) * (a->n / bn);
     if (tiles > 0x7fffffffLL) return fail(FDS_ERR_INVALID_ARGUMENT, "too many tiles");
 
-    CUtensorMap ma, mb;
+    CUtensorMap ma, mb, mo;
     if ((rc = make_matrix_map(&ma, a->a, a->dtype, a->k, a->m, a->a_row_stride, fds::gemm::kBM)) != FDS_OK) return rc;
     if ((rc = make_matrix_map(&mb, a->w, a->dtype, a->k, a->n, a->w_row_stride, bn)) != FDS_OK) return rc;
+    if ((rc = make_out_map(&mo, a->out, f32_out, a->dtype, a->n, a->m, a->out_row_stride)) != FDS_OK) return rc;
     fds::gemm::Params p{};
-    p.out = a->out;
-    p.out_stride = a->out_row_stride;
     p.bias = a->bias;
     p.cos_t = a->cos;
     p.sin_t = a->sin;
@@ -617,11 +636,11 @@ int fds_linear_fwd(const FdsLinearArgs* a, void* stream) {
     const int grid = static_cast<int>(tiles < ctas ? tiles : ctas);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (a->dtype == FDS_DTYPE_FP16)
-        rc = bn == 256 ? launch_gemm_epi<__half, 256>(a->epilogue, ma, mb, p, grid, s)
-                       : launch_gemm_epi<__half, 128>(a->epilogue, ma, mb, p, grid, s);
+        rc = bn == 256 ? launch_gemm_epi<__half, 256>(a->epilogue, ma, mb, mo, p, grid, s)
+                       : launch_gemm_epi<__half, 128>(a->epilogue, ma, mb, mo, p, grid, s);
     else
-        rc = bn == 256 ? launch_gemm_epi<__nv_bfloat16, 256>(a->epilogue, ma, mb, p, grid, s)
-                       : launch_gemm_epi<__nv_bfloat16, 128>(a->epilogue, ma, mb, p, grid, s);
+        rc = bn == 256 ? launch_gemm_epi<__nv_bfloat16, 256>(a->epilogue, ma, mb, mo, p, grid, s)
+                       : launch_gemm_epi<__nv_bfloat16, 128>(a->epilogue, ma, mb, mo, p, grid, s);
     return rc == FDS_OK ? ok() : rc;
 }
 

@@ -18,11 +18,13 @@
 //   warp 2      TMEM owner (allocates / releases the 2 x BN columns)
 //   warp 3      idle
 //   warps 4-11  epilogue: thread = output row = TMEM lane; two warps per lane
-//               quarter, each taking half of the tile's columns, the next
-//               chunk's TMEM load and bias in flight while one is written out
+//               quarter, each taking half of the tile's columns. A warp turns
+//               128 bytes of each of its 32 rows at a time into a swizzled
+//               shared-memory box and one lane hands the box to TMA: a store
+//               (kStore, kRope) or an add into the fp32 residual done in L2
+//               (kAccum), so the SM writes whole lines and never reads x
 // The accumulator is double-buffered in TMEM, so the epilogue of tile i runs
-// under the MMAs of tile i + 1 (the epilogue is latency-bound: it needs the
-// warps). Every wait is bounded (see attn_kernel.cuh).
+// under the MMAs of tile i + 1. Every wait is bounded (see attn_kernel.cuh).
 #pragma once
 
 #include <cuda.h>
@@ -54,7 +56,11 @@ struct Smem {
     static constexpr int b_bytes = BN * kBK * 2;
     static constexpr int a = 0;
     static constexpr int b = a + kStages * a_bytes;
-    static constexpr int bars = b + kStages * b_bytes;
+    // one staging box per epilogue warp: 32 rows x 128 bytes, 1024-aligned (the
+    // 128-byte swizzle repeats every 8 rows)
+    static constexpr int kStgBytes = 32 * 128;
+    static constexpr int stg = b + kStages * b_bytes;
+    static constexpr int bars = stg + kEpiWarps * kStgBytes;
     static constexpr int kFull = 0;                 // [stage] A and W tiles landed
     static constexpr int kEmpty = kFull + kStages;  // [stage] MMAs done with the stage
     static constexpr int kAccFull = kEmpty + kStages;    // [buffer] tile's accumulator complete
@@ -69,8 +75,6 @@ struct Smem {
 };
 
 struct Params {
-    void* out;
-    int64_t out_stride;       // elements
     const void* bias;         // [N] operand type, or null
     const float* cos_t;       // kRope: fp32 [>= seq_len, 64]
     const float* sin_t;
@@ -113,22 +117,28 @@ __device__ __forceinline__ float bias_at(const uint4 (&raw)[4], int c) {
     return to_f<T>(reinterpret_cast<const T*>(&raw[c >> 3])[c & 7]);
 }
 
-template <typename T>
-__device__ __forceinline__ void store32(T* dst, const float (&v)[32]) {
+// This lane's 128-byte row of its warp's staging box (16-byte chunk j at chunk
+// j ^ (row & 7): the tensor map's 128-byte swizzle, and no two lanes of a
+// quarter-warp on the same banks), written once the box's previous contents
+// have been read out by TMA (lane 0 issued those copies). The writes are then
+// made visible to the async proxy for the copy lane 0 issues next.
+__device__ __forceinline__ void stage_row(uint32_t srow, int lane, const uint32_t (&w)[32]) {
+    if (lane == 0) bulk_wait_read_all();
+    __syncwarp();
+    const int sw = lane & 7;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        uint4 u;
-        u.x = DTypeTraits<T>::pack(v[8 * q + 0], v[8 * q + 1]);
-        u.y = DTypeTraits<T>::pack(v[8 * q + 2], v[8 * q + 3]);
-        u.z = DTypeTraits<T>::pack(v[8 * q + 4], v[8 * q + 5]);
-        u.w = DTypeTraits<T>::pack(v[8 * q + 6], v[8 * q + 7]);
-        reinterpret_cast<uint4*>(dst)[q] = u;
-    }
+    for (int j = 0; j < 8; ++j)
+        st_shared_v4(srow + (static_cast<uint32_t>(j ^ sw) << 4),
+                     make_int4(static_cast<int>(w[4 * j]), static_cast<int>(w[4 * j + 1]),
+                               static_cast<int>(w[4 * j + 2]), static_cast<int>(w[4 * j + 3])));
+    fence_proxy_async_smem();
+    __syncwarp();
 }
 
 template <typename T, int BN, int kEpi>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, const Params p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                const __grid_constant__ CUtensorMap map_out, const Params p) {
     using S = Smem<BN>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -163,6 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0 && lane == 0) {
         prefetch_tensormap(&map_a);
         prefetch_tensormap(&map_b);
+        prefetch_tensormap(&map_out);
     }
     if (warp == 2) {
         tmem_alloc(tmem_holder, 2 * BN);
@@ -244,79 +255,55 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int c_begin = ((warp - kEpiWarp0) >> 2) * (BN / 2);  // this warp's column half
         const int row = wq * 32 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(wq * 32) << 16;
+        const uint32_t stg = sbase + S::stg + (warp - kEpiWarp0) * S::kStgBytes;
+        const uint32_t srow = stg + lane * 128;
         const T* bias = static_cast<const T*>(p.bias);
         int lt = 0;
         bool ok = true;
         for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x, ++lt) {
             const int buf = lt & 1;
             const int m0 = (t / p.tiles_n) * kBM, n0 = (t % p.tiles_n) * BN;
-            const int m = m0 + row;
-            const bool valid = m < p.m;
-            // kAccum: the residual rows do not depend on the product, so the
-            // first chunk's are read while the MMAs still run
-            float4 xr[2][8];
-            float* xrow = static_cast<float*>(p.out) + static_cast<int64_t>(m) * p.out_stride + n0;
-            if constexpr (kEpi == kAccum) {
-                if (valid) {
-#pragma unroll
-                    for (int r = 0; r < 8; ++r) xr[0][r] = reinterpret_cast<const float4*>(xrow + c_begin)[r];
-                }
-            }
+            const int y0 = m0 + wq * 32;     // the warp's first row; rows >= m are clipped by TMA
+            const bool live = y0 < p.m;      // a box wholly past the last row is not copied
             ok = warp_wait(bar(S::kAccFull + buf), (lt >> 1) & 1, ctl, FDS_STATUS_TIMEOUT_SOFTMAX);
             if (!ok) break;
             tc_fence_after();
             const uint32_t tacc = tmem + lane_addr + buf * BN;
             if constexpr (kEpi == kAccum) {
-                // 32 columns at a time; the next chunk's residual rows in flight
-#pragma unroll
+                // fp32 boxes of 32 columns, added into the residual by TMA
+#pragma unroll 1
                 for (int q = 0; q < BN / 64; ++q) {
                     const int c = c_begin + 32 * q;
                     uint32_t acc[32];
                     uint4 braw[4];
                     tmem_ld32(tacc + c, acc);
                     fetch_bias32<T>(bias, n0 + c, braw);
-                    if (q + 1 < BN / 64 && valid) {
-#pragma unroll
-                        for (int r = 0; r < 8; ++r)
-                            xr[(q + 1) & 1][r] = reinterpret_cast<const float4*>(xrow + c + 32)[r];
-                    }
                     tmem_wait_ld();
-                    if (valid) {
-                        float4* dst = reinterpret_cast<float4*>(xrow + c);
+                    if (q + 1 == BN / 64) warp_arrive(bar(S::kAccEmpty + buf), lane);  // accumulator read out
+                    uint32_t w[32];
 #pragma unroll
-                        for (int r = 0; r < 8; ++r) {
-                            float4 x = xr[q & 1][r];
-                            x.x += __uint_as_float(acc[4 * r]) + bias_at<T>(braw, 4 * r);
-                            x.y += __uint_as_float(acc[4 * r + 1]) + bias_at<T>(braw, 4 * r + 1);
-                            x.z += __uint_as_float(acc[4 * r + 2]) + bias_at<T>(braw, 4 * r + 2);
-                            x.w += __uint_as_float(acc[4 * r + 3]) + bias_at<T>(braw, 4 * r + 3);
-                            dst[r] = x;
-                        }
+                    for (int d = 0; d < 32; ++d) w[d] = __float_as_uint(__uint_as_float(acc[d]) + bias_at<T>(braw, d));
+                    stage_row(srow, lane, w);
+                    if (lane == 0 && live) {
+                        tma_reduce_add_2d(&map_out, stg, n0 + c, y0);
+                        bulk_commit_group();
                     }
                 }
             } else if constexpr (kEpi == kRope) {
-                // one 64-column head at a time (both halves of the rotation);
-                // cos / sin repeat every 32 columns (cat([f, f])): this row's 32
-                // pairs are read once per tile and serve every head
-                const bool rot = valid && n0 + c_begin < p.rope_cols;
-                float cs[32], sn[32];
-                if (rot) {
-                    const int pos = m % p.seq_len;
-                    const float4* cr = reinterpret_cast<const float4*>(p.cos_t + static_cast<int64_t>(pos) * 64);
-                    const float4* sr = reinterpret_cast<const float4*>(p.sin_t + static_cast<int64_t>(pos) * 64);
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const float4 c4 = __ldg(cr + q), s4 = __ldg(sr + q);
-                        cs[4 * q] = c4.x, cs[4 * q + 1] = c4.y, cs[4 * q + 2] = c4.z, cs[4 * q + 3] = c4.w;
-                        sn[4 * q] = s4.x, sn[4 * q + 1] = s4.y, sn[4 * q + 2] = s4.z, sn[4 * q + 3] = s4.w;
-                    }
-                }
+                // one 64-column head per box (both halves of the rotation);
+                // cos / sin repeat every 32 columns (cat([f, f])): every head of
+                // the row reads the same 32 pairs (L1 hits after the first)
+                const bool rot = n0 + c_begin < p.rope_cols;
+                const int pos = (m0 + row) % p.seq_len;
+                const float4* cr = reinterpret_cast<const float4*>(p.cos_t + static_cast<int64_t>(pos) * 64);
+                const float4* sr = reinterpret_cast<const float4*>(p.sin_t + static_cast<int64_t>(pos) * 64);
 #pragma unroll 1
                 for (int c = c_begin; c < c_begin + BN / 2; c += 64) {
+                    uint32_t w[32];  // the head's row: w[k] = columns 2k, 2k + 1
 #pragma unroll
                     for (int d0 = 0; d0 < 32; d0 += 16) {  // pairs (d, d + 32), 16 at a time
                         uint32_t lo[16], hi[16];
-                        uint4 bl[4], bh[4];
+                        uint4 bl[2], bh[2];
                         tmem_ld16(tacc + c + d0, lo);
                         tmem_ld16(tacc + c + 32 + d0, hi);
 #pragma unroll
@@ -331,59 +318,67 @@ __global__ void __launch_bounds__(kThreads, 1)
                         float a[16], b[16];
 #pragma unroll
                         for (int d = 0; d < 16; ++d) {
-                            a[d] = round_t<T>(__uint_as_float(lo[d]) + bias_at<T>(bl, d));
-                            b[d] = round_t<T>(__uint_as_float(hi[d]) + bias_at<T>(bh, d));
+                            a[d] = round_t<T>(__uint_as_float(lo[d]) + to_f<T>(reinterpret_cast<const T*>(bl)[d]));
+                            b[d] = round_t<T>(__uint_as_float(hi[d]) + to_f<T>(reinterpret_cast<const T*>(bh)[d]));
                         }
                         if (rot) {
 #pragma unroll
-                            for (int d = 0; d < 16; ++d) {
-                                const float x1 = a[d], x2 = b[d];
-                                a[d] = x1 * cs[d0 + d] - x2 * sn[d0 + d];
-                                b[d] = x2 * cs[d0 + d] + x1 * sn[d0 + d];
-                            }
-                        }
-                        if (valid) {
-                            T* dst = static_cast<T*>(p.out) + static_cast<int64_t>(m) * p.out_stride + n0 + c + d0;
+                            for (int q = 0; q < 4; ++q) {
+                                const float4 c4 = __ldg(cr + d0 / 4 + q), s4 = __ldg(sr + d0 / 4 + q);
+                                const float cq[4] = {c4.x, c4.y, c4.z, c4.w}, sq[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
-                            for (int q = 0; q < 2; ++q) {
-                                uint4 u, w;
-                                u.x = DTypeTraits<T>::pack(a[8 * q + 0], a[8 * q + 1]);
-                                u.y = DTypeTraits<T>::pack(a[8 * q + 2], a[8 * q + 3]);
-                                u.z = DTypeTraits<T>::pack(a[8 * q + 4], a[8 * q + 5]);
-                                u.w = DTypeTraits<T>::pack(a[8 * q + 6], a[8 * q + 7]);
-                                w.x = DTypeTraits<T>::pack(b[8 * q + 0], b[8 * q + 1]);
-                                w.y = DTypeTraits<T>::pack(b[8 * q + 2], b[8 * q + 3]);
-                                w.z = DTypeTraits<T>::pack(b[8 * q + 4], b[8 * q + 5]);
-                                w.w = DTypeTraits<T>::pack(b[8 * q + 6], b[8 * q + 7]);
-                                reinterpret_cast<uint4*>(dst)[q] = u;
-                                reinterpret_cast<uint4*>(dst + 32)[q] = w;
+                                for (int e = 0; e < 4; ++e) {
+                                    const int d = 4 * q + e;
+                                    const float x1 = a[d], x2 = b[d];
+                                    a[d] = x1 * cq[e] - x2 * sq[e];
+                                    b[d] = x2 * cq[e] + x1 * sq[e];
+                                }
                             }
                         }
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            w[d0 / 2 + q] = DTypeTraits<T>::pack(a[2 * q], a[2 * q + 1]);
+                            w[16 + d0 / 2 + q] = DTypeTraits<T>::pack(b[2 * q], b[2 * q + 1]);
+                        }
+                    }
+                    if (c + 64 == c_begin + BN / 2) warp_arrive(bar(S::kAccEmpty + buf), lane);
+                    stage_row(srow, lane, w);
+                    if (lane == 0 && live) {
+                        tma_store_2d(&map_out, stg, n0 + c, y0);
+                        bulk_commit_group();
                     }
                 }
             } else {
-                // kStore: 32 columns at a time, the next chunk's TMEM load and bias in flight
-                uint32_t acc[2][32];
-                uint4 braw[2][4];
-                tmem_ld32(tacc + c_begin, acc[0]);
-                fetch_bias32<T>(bias, n0 + c_begin, braw[0]);
-#pragma unroll
-                for (int q = 0; q < BN / 64; ++q) {
-                    const int c = c_begin + 32 * q;
+                // kStore: 64-column boxes
+#pragma unroll 1
+                for (int c = c_begin; c < c_begin + BN / 2; c += 64) {
+                    uint32_t a0[32], a1[32];
+                    uint4 b0[4], b1[4];
+                    tmem_ld32(tacc + c, a0);
+                    tmem_ld32(tacc + c + 32, a1);
+                    fetch_bias32<T>(bias, n0 + c, b0);
+                    fetch_bias32<T>(bias, n0 + c + 32, b1);
                     tmem_wait_ld();
-                    if (q + 1 < BN / 64) {
-                        tmem_ld32(tacc + c + 32, acc[(q + 1) & 1]);
-                        fetch_bias32<T>(bias, n0 + c + 32, braw[(q + 1) & 1]);
-                    }
-                    float v[32];
+                    if (c + 64 == c_begin + BN / 2) warp_arrive(bar(S::kAccEmpty + buf), lane);
+                    uint32_t w[32];
 #pragma unroll
-                    for (int d = 0; d < 32; ++d) v[d] = __uint_as_float(acc[q & 1][d]) + bias_at<T>(braw[q & 1], d);
-                    if (valid)
-                        store32<T>(static_cast<T*>(p.out) + static_cast<int64_t>(m) * p.out_stride + n0 + c, v);
+                    for (int q = 0; q < 16; ++q) {
+                        w[q] = DTypeTraits<T>::pack(__uint_as_float(a0[2 * q]) + bias_at<T>(b0, 2 * q),
+                                                    __uint_as_float(a0[2 * q + 1]) + bias_at<T>(b0, 2 * q + 1));
+                        w[16 + q] = DTypeTraits<T>::pack(__uint_as_float(a1[2 * q]) + bias_at<T>(b1, 2 * q),
+                                                         __uint_as_float(a1[2 * q + 1]) + bias_at<T>(b1, 2 * q + 1));
+                    }
+                    stage_row(srow, lane, w);
+                    if (lane == 0 && live) {
+                        tma_store_2d(&map_out, stg, n0 + c, y0);
+                        bulk_commit_group();
+                    }
                 }
             }
-            warp_arrive(bar(S::kAccEmpty + buf), lane);  // the MMA warp may reuse this accumulator
         }
+        // the copies out of the staging boxes have landed before the CTA exits
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
     }
     __syncwarp();
     tc_fence_before();
