@@ -544,57 +544,65 @@ def linear_leg(device: torch.device, steps: int = 20) -> dict:
     """The projections either side of the attention on this library's tcgen05
     GEMM, at the config-2 / config-4 shapes (L = 6000): the encoder QKV
     projection with bias, the DiT QKV projection with the RoPE epilogue, the
-    out-projection accumulated into the fp32 residual. Each timed eagerly with
-    CUDA events over `steps` launches after 3 warm-up launches; torch's F.linear
-    (cuBLAS) on the same operands beside it for context. Algorithmic FLOPs
-    2 M N K; frac against the measured cuBLAS bf16 burst peak."""
-    import torch.nn.functional as Fn
-
+    out-projection accumulated into the fp32 residual. Eight operand sets (more
+    bytes than L2 holds) are cycled through one CUDA graph of eight calls; device
+    time per call from CUDA events over `steps` replays after 3 warm-up
+    replays, with torch (cuBLAS) on the same operands the same way for context.
+    Algorithmic FLOPs 2 M N K; frac against the measured cuBLAS bf16 burst peak.
+    ``pair`` / ``single``: this library with 256-row tiles over CTA pairs (the
+    default) / 128-row tiles on one CTA each."""
     import fastdialoguesidon_b200 as F
 
     g = torch.Generator(device=device).manual_seed(17)
     peak, _ = measured_peak()
+    sets = 8
 
-    def timed(fn) -> float:
-        for _ in range(3):
-            fn()
-        torch.cuda.synchronize(device)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(steps):
-            fn()
-        e1.record()
-        torch.cuda.synchronize(device)
-        return e0.elapsed_time(e1) / steps
+    def timed(calls) -> float:
+        def body():
+            for c in calls:
+                c()
+        return time_graph(body, steps, 3, device, False) / steps / len(calls)
 
     res = {}
     cases = (("encoder_qkv", 1024, 3072, "store"), ("dit_qkv_rope", 768, 2304, "rope"),
              ("encoder_out_accumulate", 1024, 1024, "accum"))
     cos, sin = F.rope_tables(L_WINDOW, device)
     for name, k, n, kind in cases:
-        x = torch.randn(L_WINDOW, k, generator=g, device=device).half()
-        w = (torch.randn(n, k, generator=g, device=device) * 0.02).half()
-        b = (torch.randn(n, generator=g, device=device) * 0.02).half()
-        flop = 2.0 * L_WINDOW * n * k
-        if kind == "store":
-            out = torch.empty(L_WINDOW, n, dtype=torch.float16, device=device)
-            ours = timed(lambda: F.linear(x, w, b, out=out))
-            ref = timed(lambda: Fn.linear(x, w, b))
-        elif kind == "rope":
-            out = torch.empty(L_WINDOW, n, dtype=torch.float16, device=device)
-            ours = timed(lambda: F.linear_rope(x, w, b, cos, sin, L_WINDOW, n // 192, out=out))
-            ref = timed(lambda: Fn.linear(x, w, b))
+        xs = [torch.randn(L_WINDOW, k, generator=g, device=device).half() for _ in range(sets)]
+        ws = [(torch.randn(n, k, generator=g, device=device) * 0.02).half() for _ in range(sets)]
+        bs = [(torch.randn(n, generator=g, device=device) * 0.02).half() for _ in range(sets)]
+        if kind == "accum":
+            outs = [torch.zeros(L_WINDOW, n, device=device) for _ in range(sets)]
         else:
-            acc = torch.zeros(L_WINDOW, n, device=device)
-            ours = timed(lambda: F.accumulate(acc, x, w))
-            ref = timed(lambda: torch.addmm(acc, x, w.t(), out_dtype=torch.float32, out=acc))
-        tf = flop / (ours * 1e-3) / 1e12
-        res[name] = {"m": L_WINDOW, "n": n, "k": k, "ms": round(ours, 4), "tflops": round(tf, 1),
-                     "frac": round(tf / peak, 3), "torch_ms": round(ref, 4),
-                     "torch_tflops": round(flop / (ref * 1e-3) / 1e12, 1)}
+            outs = [torch.empty(L_WINDOW, n, dtype=torch.float16, device=device) for _ in range(sets)]
+        flop = 2.0 * L_WINDOW * n * k
+
+        def ours(i, pair):
+            x, w, b, o = xs[i], ws[i], bs[i], outs[i]
+            if kind == "store":
+                return lambda: F.linear(x, w, b, out=o, pair=pair)
+            if kind == "rope":
+                return lambda: F.linear_rope(x, w, b, cos, sin, L_WINDOW, n // 192, out=o, pair=pair)
+            return lambda: F.accumulate(o, x, w, pair=pair)
+
+        def ref(i):
+            x, w, b, o = xs[i], ws[i], bs[i], outs[i]
+            if kind == "accum":
+                return lambda: torch.addmm(o, x, w.t(), out_dtype=torch.float32, out=o)
+            return lambda: torch.addmm(b, x, w.t(), out=o)
+
+        pair_ms = timed([ours(i, None) for i in range(sets)])
+        single_ms = timed([ours(i, False) for i in range(sets)])
+        torch_ms = timed([ref(i) for i in range(sets)])
+        tf = flop / (pair_ms * 1e-3) / 1e12
+        res[name] = {"m": L_WINDOW, "n": n, "k": k, "ms": round(pair_ms, 4), "tflops": round(tf, 1),
+                     "frac": round(tf / peak, 3), "single_cta_ms": round(single_ms, 4),
+                     "torch_ms": round(torch_ms, 4), "torch_tflops": round(flop / (torch_ms * 1e-3) / 1e12, 1)}
     F.check_status(device)
-    res["note"] = ("tcgen05 GEMM of this library (fds_linear_fwd); torch_ms: torch.nn.functional.linear / "
-                   "torch.addmm (cuBLAS) on the same operands, the reference's own call at these sites")
+    res["note"] = ("tcgen05 GEMM of this library (fds_linear_fwd), 256-row tiles over CTA pairs; single_cta_ms: "
+                   "128-row tiles, one CTA each; torch_ms: torch.addmm (cuBLAS) on the same operands, the "
+                   "reference's own call at these sites (rope: without the reference's separate rope_split pass); "
+                   "device time per call inside a CUDA graph cycling 8 operand sets (> L2)")
     return res
 
 

@@ -33,8 +33,11 @@ FDS_ROPE_STATIC_SCRATCH_BYTES = 20 * 1024 * 1024
 FDS_EPILOGUE_STORE = 0
 FDS_EPILOGUE_ROPE = 1
 FDS_EPILOGUE_ACCUMULATE_F32 = 2
+FDS_GEMM_AUTO = 0
+FDS_GEMM_SINGLE = 1
+FDS_GEMM_PAIR = 2
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 # every symbol include/fds_b200.h declares (checked by the CPU test suite)
 EXPORTED_SYMBOLS = (
@@ -149,6 +152,7 @@ class FdsLinearArgs(ctypes.Structure):
         ("rope_cols", ctypes.c_int32),
         ("timeout_ns", ctypes.c_int64),
         ("grid_ctas", ctypes.c_int32),
+        ("cta_pair", ctypes.c_int32),
     ]
 
 

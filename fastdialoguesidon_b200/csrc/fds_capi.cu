@@ -5,6 +5,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdlib>
@@ -332,38 +333,103 @@ int fds_detail::set_error(int code, const char* fmt, ...) {
 
 namespace {
 
-template <typename T, int BN, int kEpi>
+// Clusters of two CTAs (the pair GEMM), with PDL like launch_pdl.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pair(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                        Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+template <typename T, int BN, int kEpi, bool kPair>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const fds::gemm::Params& p,
                 int grid, cudaStream_t stream) {
-    auto kern = fds::gemm::gemm_kernel<T, BN, kEpi>;
-    constexpr int smem = fds::gemm::Smem<BN>::alloc;
+    auto kern = fds::gemm::gemm_kernel<T, BN, kEpi, kPair>;
+    constexpr int smem = fds::gemm::Smem<BN, kPair>::alloc;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "cudaFuncSetAttribute(gemm): %s", cudaGetErrorString(e));
-    e = launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(fds::gemm::kThreads), smem, stream, ma, mb, mo, p);
+    const dim3 g(static_cast<unsigned>(grid)), b(fds::gemm::kThreads);
+    e = kPair ? launch_pair(kern, g, b, smem, stream, ma, mb, mo, p) : launch_pdl(kern, g, b, smem, stream, ma, mb, mo, p);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "linear launch: %s", cudaGetErrorString(e));
     return FDS_OK;
 }
 
-template <typename T, int BN>
+template <typename T, int BN, bool kPair>
 int launch_gemm_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo,
                     const fds::gemm::Params& p, int grid, cudaStream_t stream) {
     switch (epi) {
-        case FDS_EPILOGUE_STORE: return launch_gemm<T, BN, fds::gemm::kStore>(ma, mb, mo, p, grid, stream);
-        case FDS_EPILOGUE_ROPE: return launch_gemm<T, BN, fds::gemm::kRope>(ma, mb, mo, p, grid, stream);
-        default: return launch_gemm<T, BN, fds::gemm::kAccum>(ma, mb, mo, p, grid, stream);
+        case FDS_EPILOGUE_STORE: return launch_gemm<T, BN, fds::gemm::kStore, kPair>(ma, mb, mo, p, grid, stream);
+        case FDS_EPILOGUE_ROPE: return launch_gemm<T, BN, fds::gemm::kRope, kPair>(ma, mb, mo, p, grid, stream);
+        default: return launch_gemm<T, BN, fds::gemm::kAccum, kPair>(ma, mb, mo, p, grid, stream);
     }
 }
 
+template <typename T>
+int launch_gemm_shape(int bn, bool pair, int epi, const CUtensorMap& ma, const CUtensorMap& mb,
+                      const CUtensorMap& mo, const fds::gemm::Params& p, int grid, cudaStream_t stream) {
+    if (pair)
+        return bn == 256 ? launch_gemm_epi<T, 256, true>(epi, ma, mb, mo, p, grid, stream)
+                         : launch_gemm_epi<T, 128, true>(epi, ma, mb, mo, p, grid, stream);
+    return bn == 256 ? launch_gemm_epi<T, 256, false>(epi, ma, mb, mo, p, grid, stream)
+                     : launch_gemm_epi<T, 128, false>(epi, ma, mb, mo, p, grid, stream);
+}
+
+// How many CTA pairs of the pair GEMM can be resident at once on the current
+// device (clusters must sit within one GPC, so this can be below SMs / 2);
+// cached per device. 0 if it cannot be queried.
+int max_pairs() {
+    static std::atomic<int> cached[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    int n = cached[dev].load(std::memory_order_relaxed);
+    if (n == 0) {
+        auto kern = fds::gemm::gemm_kernel<__half, 256, fds::gemm::kStore, true>;
+        constexpr int smem = fds::gemm::Smem<256, true>::alloc;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return 0;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2);
+        cfg.blockDim = dim3(fds::gemm::kThreads);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            return 0;
+        }
+        cached[dev].store(n, std::memory_order_relaxed);
+    }
+    return n;
+}
+
 // Output tile width: 256 columns (more reuse of each A tile) unless n is not a
-// multiple of 256 or 128-column tiles fill the last wave clearly better.
-int choose_bn(int64_t m, int64_t n, int64_t ctas) {
+// multiple of 256 or 128-column tiles fill the last wave of tiles over the
+// launched CTAs (pairs) clearly better (measured at n = 1024, m = 6000).
+int choose_bn(int64_t m, int64_t n, int64_t units, int tile_m) {
     if (n % 256 != 0) return 128;
-    const int64_t mt = (m + fds::gemm::kBM - 1) / fds::gemm::kBM;
+    const int64_t mt = (m + tile_m - 1) / tile_m;
     const auto fill = [&](int64_t bn) {
         const int64_t tiles = mt * (n / bn);
-        const int64_t waves = (tiles + ctas - 1) / ctas;
-        return static_cast<double>(tiles) / static_cast<double>(waves * ctas);
+        const int64_t waves = (tiles + units - 1) / units;
+        return static_cast<double>(tiles) / static_cast<double>(waves * units);
     };
     return fill(128) > fill(256) + 0.1 ? 128 : 256;
 }
@@ -610,14 +676,37 @@ int fds_linear_fwd(const FdsLinearArgs* a, void* stream) {
     const int sms = sm_count();
     if (a->grid_ctas < 0 || (a->grid_ctas > 0 && sms > 0 && a->grid_ctas > sms))
         return fail(FDS_ERR_INVALID_ARGUMENT, "grid_ctas must be in [0, %d] (got %d)", sms, a->grid_ctas);
-    const int64_t ctas = a->grid_ctas > 0 ? a->grid_ctas : (sms > 0 ? sms : 148);
-    const int bn = choose_bn(a->m, a->n, ctas);
-    const int64_t tiles = static_cast<int64_t>((a->m + fds::gemm::kBM - 1) / fds::gemm::kBM) * (a->n / bn);
+    if (a->cta_pair < FDS_GEMM_AUTO || a->cta_pair > FDS_GEMM_PAIR)
+        return fail(FDS_ERR_INVALID_ARGUMENT, "cta_pair must be FDS_GEMM_AUTO, FDS_GEMM_SINGLE or FDS_GEMM_PAIR");
+    int64_t ctas = a->grid_ctas > 0 ? a->grid_ctas : (sms > 0 ? sms : 148);
+    // CTA pairs (256-row tiles) unless asked otherwise, there is only one
+    // 128-row tile of output rows, k is short (below 512 the pair's extra set-up
+    // and cluster barriers are not repaid), the epilogue is RoPE (it, not the
+    // k-loop, bounds the kernel, and a pair waits for the slower of its two
+    // CTAs' epilogues) -- both measured at m = 6000 -- or no pair can be placed
+    bool pair = a->cta_pair == FDS_GEMM_PAIR ||
+                (a->cta_pair == FDS_GEMM_AUTO && a->m > fds::gemm::kBM && a->k >= 512 &&
+                 a->epilogue != FDS_EPILOGUE_ROPE);
+    if (pair) {
+        const int64_t pairs = std::min<int64_t>(ctas / 2, max_pairs());
+        if (pairs < 1) {
+            if (a->cta_pair == FDS_GEMM_PAIR)
+                return fail(FDS_ERR_INVALID_ARGUMENT, "no CTA pair can be launched (grid_ctas %d)", a->grid_ctas);
+            pair = false;
+        } else {
+            ctas = 2 * pairs;
+        }
+    }
+    const int tile_m = pair ? 2 * fds::gemm::kBM : fds::gemm::kBM;
+    const int64_t units = pair ? ctas / 2 : ctas;
+    const int bn = choose_bn(a->m, a->n, units, tile_m);
+    const int64_t tiles = static_cast<int64_t>((a->m + tile_m - 1) / tile_m) * (a->n / bn);
     if (tiles > 0x7fffffffLL) return fail(FDS_ERR_INVALID_ARGUMENT, "too many tiles");
 
     CUtensorMap ma, mb, mo;
     if ((rc = make_matrix_map(&ma, a->a, a->dtype, a->k, a->m, a->a_row_stride, fds::gemm::kBM)) != FDS_OK) return rc;
-    if ((rc = make_matrix_map(&mb, a->w, a->dtype, a->k, a->n, a->w_row_stride, bn)) != FDS_OK) return rc;
+    if ((rc = make_matrix_map(&mb, a->w, a->dtype, a->k, a->n, a->w_row_stride, pair ? bn / 2 : bn)) != FDS_OK)
+        return rc;
     if ((rc = make_out_map(&mo, a->out, f32_out, a->dtype, a->n, a->m, a->out_row_stride)) != FDS_OK) return rc;
     fds::gemm::Params p{};
     p.bias = a->bias;
@@ -633,14 +722,10 @@ int fds_linear_fwd(const FdsLinearArgs* a, void* stream) {
     p.rope_cols = a->epilogue == FDS_EPILOGUE_ROPE ? a->rope_cols : 0;
     p.tiles_n = a->n / bn;
     p.tiles = static_cast<int32_t>(tiles);
-    const int grid = static_cast<int>(tiles < ctas ? tiles : ctas);
+    const int grid = static_cast<int>((tiles < units ? tiles : units) * (pair ? 2 : 1));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (a->dtype == FDS_DTYPE_FP16)
-        rc = bn == 256 ? launch_gemm_epi<__half, 256>(a->epilogue, ma, mb, mo, p, grid, s)
-                       : launch_gemm_epi<__half, 128>(a->epilogue, ma, mb, mo, p, grid, s);
-    else
-        rc = bn == 256 ? launch_gemm_epi<__nv_bfloat16, 256>(a->epilogue, ma, mb, mo, p, grid, s)
-                       : launch_gemm_epi<__nv_bfloat16, 128>(a->epilogue, ma, mb, mo, p, grid, s);
+    rc = a->dtype == FDS_DTYPE_FP16 ? launch_gemm_shape<__half>(bn, pair, a->epilogue, ma, mb, mo, p, grid, s)
+                                    : launch_gemm_shape<__nv_bfloat16>(bn, pair, a->epilogue, ma, mb, mo, p, grid, s);
     return rc == FDS_OK ? ok() : rc;
 }
 

@@ -10,11 +10,17 @@
 //   kAccum   out (fp32) += D (+ bias)                        (x += a W^T into
 //            the fp32 residual stream, torch.addmm(out_dtype=fp32, out=x))
 //
-// Persistent CTAs, one per SM at most, walk the 128 x BN output tiles in a
-// static stride. Warp roles (384 threads):
+// Persistent CTAs, one per SM at most, walk the output tiles in a static
+// stride: 128 x BN tiles, one per CTA, or (kPair) 256 x BN tiles over a
+// cluster of two CTAs that share each tensor-core operation (tcgen05
+// cta_group::2: each CTA loads its own 128 rows of A and half of the tile's W
+// rows, so a CTA moves 32 KB per 64-deep k-block of a 256-wide tile instead of
+// 48 KB; the even CTA issues the MMAs, each CTA's TMEM holds its own 128 output
+// rows). Warp roles (384 threads):
 //   warp 0      TMA producer: A / W tiles of BK = 64 columns into a 4-stage ring
-//   warp 1      MMA issuer (one elected lane): tcgen05.mma kind::f16, M = 128,
-//               N = BN, K = 16, fp32 accumulators in TMEM
+//   warp 1      MMA issuer (one elected lane; the even CTA of a pair):
+//               tcgen05.mma kind::f16, M = 128 (256 for a pair), N = BN,
+//               K = 16, fp32 accumulators in TMEM
 //   warp 2      TMEM owner (allocates / releases the 2 x BN columns)
 //   warp 3      idle
 //   warps 4-11  epilogue: thread = output row = TMEM lane; two warps per lane
@@ -45,15 +51,15 @@ constexpr int kEpiWarps = 8;
 
 enum Epi : int { kStore = 0, kRope = 1, kAccum = 2 };
 
-// The ring is as deep as shared memory allows (6 stages of 32 KB for 128-wide
-// tiles, 4 of 48 KB for 256-wide ones): the copies in flight have to cover the
-// L2 / HBM latency of a stage while the tensor cores eat one stage per
-// 256 / 512 cycles.
-template <int BN>
+// The ring is as deep as 192 KB allows (a stage is a 128 x 64 A tile and this
+// CTA's W rows): the copies in flight have to cover the L2 / HBM latency of a
+// stage while the tensor cores eat one stage per 256 / 512 cycles.
+template <int BN, bool kPair>
 struct Smem {
-    static constexpr int kStages = BN == 128 ? 6 : 4;
+    static constexpr int kBNc = kPair ? BN / 2 : BN;  // W rows this CTA loads per tile
     static constexpr int a_bytes = kBM * kBK * 2;
-    static constexpr int b_bytes = BN * kBK * 2;
+    static constexpr int b_bytes = kBNc * kBK * 2;
+    static constexpr int kStages = (192 * 1024) / (a_bytes + b_bytes);
     static constexpr int a = 0;
     static constexpr int b = a + kStages * a_bytes;
     // one staging box per epilogue warp: 32 rows x 128 bytes, 1024-aligned (the
@@ -61,10 +67,10 @@ struct Smem {
     static constexpr int kStgBytes = 32 * 128;
     static constexpr int stg = b + kStages * b_bytes;
     static constexpr int bars = stg + kEpiWarps * kStgBytes;
-    static constexpr int kFull = 0;                 // [stage] A and W tiles landed
+    static constexpr int kFull = 0;                 // [stage] A and W tiles landed (a pair: both CTAs', on the even CTA)
     static constexpr int kEmpty = kFull + kStages;  // [stage] MMAs done with the stage
     static constexpr int kAccFull = kEmpty + kStages;    // [buffer] tile's accumulator complete
-    static constexpr int kAccEmpty = kAccFull + 2;       // [buffer] epilogue read it out
+    static constexpr int kAccEmpty = kAccFull + 2;       // [buffer] epilogue read it out (a pair: both CTAs', on the even CTA)
     static constexpr int kDrain = kAccEmpty + 2;
     static constexpr int kNumBars = kDrain + 1;
     // misc block, same offsets as the attention kernel's (the bounded waits read
@@ -72,6 +78,7 @@ struct Smem {
     static constexpr int misc = bars + kNumBars * 8;
     static constexpr int total = misc + 48;
     static constexpr int alloc = total + 1024;
+    static_assert(stg % 1024 == 0 && alloc <= 227 * 1024, "shared-memory layout");
 };
 
 struct Params {
@@ -85,7 +92,7 @@ struct Params {
     int32_t seq_len;          // kRope: position = row % seq_len
     int32_t rope_cols;        // kRope: columns [0, rope_cols) are rotated
     int32_t tiles_n;          // N / BN
-    int32_t tiles;            // ceil(M / 128) * tiles_n
+    int32_t tiles;            // ceil(M / tile rows) * tiles_n
 };
 
 template <typename T>
@@ -135,11 +142,15 @@ __device__ __forceinline__ void stage_row(uint32_t srow, int lane, const uint32_
     __syncwarp();
 }
 
-template <typename T, int BN, int kEpi>
+template <typename T, int BN, int kEpi, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const __grid_constant__ CUtensorMap map_out, const Params p) {
-    using S = Smem<BN>;
+    using S = Smem<BN, kPair>;
+    constexpr int kTileM = kPair ? 2 * kBM : kBM;
+    const uint32_t rank = kPair ? cluster_ctarank() : 0u;  // 0: the CTA that issues the MMAs
+    const int unit0 = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+    const int units = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     const uint32_t sbase = (raw_addr + 1023u) & ~1023u;
@@ -160,7 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&bars[S::kAccFull + b], 1);
-            mbar_init(&bars[S::kAccEmpty + b], kEpiWarps);  // one arrival per epilogue warp
+            mbar_init(&bars[S::kAccEmpty + b], kPair ? 2 * kEpiWarps : kEpiWarps);  // one per epilogue warp
         }
         mbar_init(&bars[S::kDrain], 1);
         st_shared_volatile_u32(ctl.misc + 4, 0);
@@ -176,21 +187,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tensormap(&map_out);
     }
     if (warp == 2) {
-        tmem_alloc(tmem_holder, 2 * BN);
-        tmem_relinquish();
+        if constexpr (kPair) {
+            tmem_alloc_pair(tmem_holder, 2 * BN);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_holder, 2 * BN);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (kPair) cluster_sync_all();  // the other CTA's barriers are initialised
     tc_fence_after();
     grid_dependency_wait();
     const uint32_t tmem = *tmem_holder;
+    // the pair's shared barriers live in the even CTA
+    const auto bar0 = [&](int idx) { return kPair ? map_to_rank(bar(idx), 0) : bar(idx); };
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         int g = 0;  // k-blocks issued
         bool ok = true;
-        for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x) {
-            const int m0 = (t / p.tiles_n) * kBM, n0 = (t % p.tiles_n) * BN;
+        for (int t = unit0; ok && t < p.tiles; t += units) {
+            // this CTA's A rows and W rows of the tile
+            const int m0 = (t / p.tiles_n) * kTileM + static_cast<int>(rank) * kBM;
+            const int n0 = (t % p.tiles_n) * BN + static_cast<int>(rank) * S::kBNc;
             for (int kb = 0; kb < kb_n; ++kb, ++g) {
                 const int st = g % S::kStages;
                 if (g >= S::kStages) {
@@ -198,27 +219,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!ok) break;
                 }
                 if (elect_one()) {
-                    mbar_arrive_expect_tx(bar(S::kFull + st), S::a_bytes + S::b_bytes);
-                    tma_load_2d(sbase + S::a + st * S::a_bytes, &map_a, bar(S::kFull + st), kb * kBK, m0);
-                    tma_load_2d(sbase + S::b + st * S::b_bytes, &map_b, bar(S::kFull + st), kb * kBK, n0);
+                    if constexpr (kPair) {
+                        // the even CTA's full barrier counts both CTAs' bytes; only it arms
+                        const uint32_t fb = map_to_rank(bar(S::kFull + st), 0);
+                        if (rank == 0) mbar_arrive_expect_tx(bar(S::kFull + st), 2 * (S::a_bytes + S::b_bytes));
+                        tma_load_2d_pair(sbase + S::a + st * S::a_bytes, &map_a, fb, kb * kBK, m0);
+                        tma_load_2d_pair(sbase + S::b + st * S::b_bytes, &map_b, fb, kb * kBK, n0);
+                    } else {
+                        mbar_arrive_expect_tx(bar(S::kFull + st), S::a_bytes + S::b_bytes);
+                        tma_load_2d(sbase + S::a + st * S::a_bytes, &map_a, bar(S::kFull + st), kb * kBK, m0);
+                        tma_load_2d(sbase + S::b + st * S::b_bytes, &map_b, bar(S::kFull + st), kb * kBK, n0);
+                    }
                 }
                 __syncwarp();
             }
         }
-        if (!ok) {
-            // aborted: let the copies already issued land before the CTA exits
+        if (!ok && rank == 0) {
+            // aborted: let the copies already armed land before the CTA exits
+            // (a pair's odd CTA has no barrier of its own to watch: its copies
+            // were issued at least one timeout before it gets here, and both
+            // CTAs meet at the cluster barrier before either exits)
             for (int s = 0; s < S::kStages; ++s) {
                 const int n_is = g > s ? (g - s + S::kStages - 1) / S::kStages : 0;
                 if (n_is > 0) wait_bounded(bar(S::kFull + s), (n_is - 1) & 1, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
             }
             __syncwarp();
         }
-    } else if (warp == 1) {
+    } else if (warp == 1 && rank == 0) {
         // ------------------------------------------------ MMA issuer
-        constexpr uint32_t idesc = idesc_f16(kBM, BN, DTypeTraits<T>::kFormat, 0, 0);
+        constexpr uint32_t idesc = idesc_f16(kTileM, BN, DTypeTraits<T>::kFormat, 0, 0);
+        // completions go to both CTAs of a pair (their stages and accumulators)
+        const auto commit = [&](int idx) {
+            if constexpr (kPair) {
+                mma_commit_pair(bar(idx));
+                mma_commit_pair(map_to_rank(bar(idx), 1));
+            } else {
+                mma_commit(bar(idx));
+            }
+        };
         int g = 0, lt = 0;
         bool ok = true, issued = false;
-        for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x, ++lt) {
+        for (int t = unit0; ok && t < p.tiles; t += units, ++lt) {
             const int buf = lt & 1;
             if (lt >= 2) {  // the epilogue has read this accumulator out
                 ok = warp_wait(bar(S::kAccEmpty + buf), ((lt >> 1) - 1) & 1, ctl, FDS_STATUS_TIMEOUT_MMA);
@@ -234,17 +275,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint64_t da = sw128_desc(sbase + S::a + st * S::a_bytes);
                     const uint64_t db = sw128_desc(sbase + S::b + st * S::b_bytes);
 #pragma unroll
-                    for (int k = 0; k < kBK / 16; ++k)
-                        mma_ss(tmem + buf * BN, da + 2 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-                    mma_commit(bar(S::kEmpty + st));
-                    if (kb + 1 == kb_n) mma_commit(bar(S::kAccFull + buf));
+                    for (int k = 0; k < kBK / 16; ++k) {
+                        if constexpr (kPair)
+                            mma_ss_pair(tmem + buf * BN, da + 2 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                        else
+                            mma_ss(tmem + buf * BN, da + 2 * k, db + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                    }
+                    commit(S::kEmpty + st);
+                    if (kb + 1 == kb_n) commit(S::kAccFull + buf);
                 }
                 __syncwarp();
                 issued = true;
             }
         }
         if (issued) {
-            if (elect_one()) mma_commit(bar(S::kDrain));
+            if (elect_one()) {
+                if constexpr (kPair)
+                    mma_commit_pair(bar(S::kDrain));
+                else
+                    mma_commit(bar(S::kDrain));
+            }
             __syncwarp();
             wait_bounded(bar(S::kDrain), 0, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
             __syncwarp();
@@ -260,9 +310,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const T* bias = static_cast<const T*>(p.bias);
         int lt = 0;
         bool ok = true;
-        for (int t = blockIdx.x; ok && t < p.tiles; t += gridDim.x, ++lt) {
+        // one arrival per warp on the (even CTA's) accumulator-empty barrier
+        const auto acc_empty = [&](int b) {
+            if constexpr (kPair) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(bar0(S::kAccEmpty + b));
+            } else {
+                warp_arrive(bar(S::kAccEmpty + b), lane);
+            }
+        };
+        for (int t = unit0; ok && t < p.tiles; t += units, ++lt) {
             const int buf = lt & 1;
-            const int m0 = (t / p.tiles_n) * kBM, n0 = (t % p.tiles_n) * BN;
+            const int m0 = (t / p.tiles_n) * kTileM + static_cast<int>(rank) * kBM, n0 = (t % p.tiles_n) * BN;
             const int y0 = m0 + wq * 32;     // the warp's first row; rows >= m are clipped by TMA
             const bool live = y0 < p.m;      // a box wholly past the last row is not copied
             ok = warp_wait(bar(S::kAccFull + buf), (lt >> 1) & 1, ctl, FDS_STATUS_TIMEOUT_SOFTMAX);
@@ -279,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_ld32(tacc + c, acc);
                     fetch_bias32<T>(bias, n0 + c, braw);
                     tmem_wait_ld();
-                    if (q + 1 == BN / 64) warp_arrive(bar(S::kAccEmpty + buf), lane);  // accumulator read out
+                    if (q + 1 == BN / 64) acc_empty(buf);  // accumulator read out
                     uint32_t w[32];
 #pragma unroll
                     for (int d = 0; d < 32; ++d) w[d] = __float_as_uint(__uint_as_float(acc[d]) + bias_at<T>(braw, d));
@@ -290,16 +350,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             } else if constexpr (kEpi == kRope) {
-                // one 64-column head per box (both halves of the rotation);
-                // cos / sin repeat every 32 columns (cat([f, f])): every head of
-                // the row reads the same 32 pairs (L1 hits after the first)
-                const bool rot = n0 + c_begin < p.rope_cols;
+                // one 64-column head per box (both halves of the rotation).
+                // cos / sin repeat every 32 columns (cat([f, f])): the row's 32
+                // pairs serve every head of the tile, so they are read once per
+                // tile (uncoalesced: a warp's lanes are 32 rows) and kept in
+                // registers; each 16-pair chunk goes straight into the staging
+                // box, so no whole head row is held
                 const int pos = (m0 + row) % p.seq_len;
-                const float4* cr = reinterpret_cast<const float4*>(p.cos_t + static_cast<int64_t>(pos) * 64);
-                const float4* sr = reinterpret_cast<const float4*>(p.sin_t + static_cast<int64_t>(pos) * 64);
+                float cs[32], sn[32];
+                if (n0 + c_begin < p.rope_cols) {
+                    const float4* cr = reinterpret_cast<const float4*>(p.cos_t + static_cast<int64_t>(pos) * 64);
+                    const float4* sr = reinterpret_cast<const float4*>(p.sin_t + static_cast<int64_t>(pos) * 64);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const float4 c4 = __ldg(cr + q), s4 = __ldg(sr + q);
+                        cs[4 * q] = c4.x, cs[4 * q + 1] = c4.y, cs[4 * q + 2] = c4.z, cs[4 * q + 3] = c4.w;
+                        sn[4 * q] = s4.x, sn[4 * q + 1] = s4.y, sn[4 * q + 2] = s4.z, sn[4 * q + 3] = s4.w;
+                    }
+                }
+                const int sw = lane & 7;
 #pragma unroll 1
                 for (int c = c_begin; c < c_begin + BN / 2; c += 64) {
-                    uint32_t w[32];  // the head's row: w[k] = columns 2k, 2k + 1
+                    const bool rot = n0 + c < p.rope_cols;
+                    if (lane == 0) bulk_wait_read_all();  // the box's previous head has been copied out
+                    __syncwarp();
 #pragma unroll
                     for (int d0 = 0; d0 < 32; d0 += 16) {  // pairs (d, d + 32), 16 at a time
                         uint32_t lo[16], hi[16];
@@ -323,26 +397,31 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         if (rot) {
 #pragma unroll
-                            for (int q = 0; q < 4; ++q) {
-                                const float4 c4 = __ldg(cr + d0 / 4 + q), s4 = __ldg(sr + d0 / 4 + q);
-                                const float cq[4] = {c4.x, c4.y, c4.z, c4.w}, sq[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-                                for (int e = 0; e < 4; ++e) {
-                                    const int d = 4 * q + e;
-                                    const float x1 = a[d], x2 = b[d];
-                                    a[d] = x1 * cq[e] - x2 * sq[e];
-                                    b[d] = x2 * cq[e] + x1 * sq[e];
-                                }
+                            for (int d = 0; d < 16; ++d) {
+                                const float x1 = a[d], x2 = b[d];
+                                a[d] = x1 * cs[d0 + d] - x2 * sn[d0 + d];
+                                b[d] = x2 * cs[d0 + d] + x1 * sn[d0 + d];
                             }
                         }
+                        // columns d0 .. d0 + 15 are 16-byte chunks d0 / 8, d0 / 8 + 1 of
+                        // the 128-byte row; columns 32 + d0 .. chunks 4 + d0 / 8, ..
 #pragma unroll
-                        for (int q = 0; q < 8; ++q) {
-                            w[d0 / 2 + q] = DTypeTraits<T>::pack(a[2 * q], a[2 * q + 1]);
-                            w[16 + d0 / 2 + q] = DTypeTraits<T>::pack(b[2 * q], b[2 * q + 1]);
+                        for (int h = 0; h < 2; ++h) {
+                            const float* v = h == 0 ? a : b;
+#pragma unroll
+                            for (int q = 0; q < 2; ++q) {
+                                const int j = 4 * h + d0 / 8 + q;
+                                st_shared_v4(srow + (static_cast<uint32_t>(j ^ sw) << 4),
+                                             make_int4(static_cast<int>(DTypeTraits<T>::pack(v[8 * q], v[8 * q + 1])),
+                                                       static_cast<int>(DTypeTraits<T>::pack(v[8 * q + 2], v[8 * q + 3])),
+                                                       static_cast<int>(DTypeTraits<T>::pack(v[8 * q + 4], v[8 * q + 5])),
+                                                       static_cast<int>(DTypeTraits<T>::pack(v[8 * q + 6], v[8 * q + 7]))));
+                            }
                         }
                     }
-                    if (c + 64 == c_begin + BN / 2) warp_arrive(bar(S::kAccEmpty + buf), lane);
-                    stage_row(srow, lane, w);
+                    if (c + 64 == c_begin + BN / 2) acc_empty(buf);
+                    fence_proxy_async_smem();
+                    __syncwarp();
                     if (lane == 0 && live) {
                         tma_store_2d(&map_out, stg, n0 + c, y0);
                         bulk_commit_group();
@@ -359,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     fetch_bias32<T>(bias, n0 + c, b0);
                     fetch_bias32<T>(bias, n0 + c + 32, b1);
                     tmem_wait_ld();
-                    if (c + 64 == c_begin + BN / 2) warp_arrive(bar(S::kAccEmpty + buf), lane);
+                    if (c + 64 == c_begin + BN / 2) acc_empty(buf);
                     uint32_t w[32];
 #pragma unroll
                     for (int q = 0; q < 16; ++q) {
@@ -383,9 +462,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     tc_fence_before();
     __syncthreads();
+    // a pair: the even CTA's MMAs into this CTA's TMEM are drained and every
+    // cross-CTA arrival has landed before either CTA releases TMEM or exits
+    if constexpr (kPair) cluster_sync_all();
     if (warp == 2) {
         tc_fence_after();
-        tmem_dealloc(tmem, 2 * BN);
+        if constexpr (kPair)
+            tmem_dealloc_pair(tmem, 2 * BN);
+        else
+            tmem_dealloc(tmem, 2 * BN);
     }
 }
 

@@ -459,7 +459,7 @@ def rotated_attention(qkv: torch.Tensor, batch: int, heads: int, out: torch.Tens
 
 def _linear_call(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, out: torch.Tensor,
                  epilogue: int, cos=None, sin=None, seq_len: int = 0, rope_cols: int = 0,
-                 timeout_ns: int = 0, grid_ctas: int = 0) -> torch.Tensor:
+                 timeout_ns: int = 0, grid_ctas: int = 0, pair: bool | None = None) -> torch.Tensor:
     _rows_operand(x, "x")
     _rows_operand(w, "w")
     m, k = x.shape
@@ -484,7 +484,8 @@ def _linear_call(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, ou
             cos=None if cos is None else cos.data_ptr(), sin=None if sin is None else sin.data_ptr(),
             status=_status(dev).data_ptr(), status_host=_status_mirror(dev).data_ptr(),
             m=m, n=n, k=k, dtype=_DTYPES[x.dtype], epilogue=epilogue, seq_len=int(seq_len),
-            rope_cols=int(rope_cols), timeout_ns=int(timeout_ns), grid_ctas=int(grid_ctas))
+            rope_cols=int(rope_cols), timeout_ns=int(timeout_ns), grid_ctas=int(grid_ctas),
+            cta_pair=N.FDS_GEMM_AUTO if pair is None else (N.FDS_GEMM_PAIR if pair else N.FDS_GEMM_SINGLE))
         rc = lib.fds_linear_fwd(ctypes.byref(args), _stream_ptr(dev))
     _raise_rc(rc, "fds_linear_fwd")
     return out
@@ -501,18 +502,24 @@ def _linear_out(x: torch.Tensor, n: int, out: torch.Tensor | None, dtype) -> tor
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None,
-           out: torch.Tensor | None = None, *, grid_ctas: int = 0) -> torch.Tensor:
+           out: torch.Tensor | None = None, *, grid_ctas: int = 0, pair: bool | None = None) -> torch.Tensor:
     """``F.linear(x, w, b)`` on the tensor cores: x [M, K], w [N, K] (nn.Linear
     layout), fp16 / bf16, fp32 accumulation, result rounded once to x's dtype.
     Reference: ``linear`` (triton/src/fds_triton/model.py:50-51), used for the
-    QKV projection before the attention (model.py:289)."""
+    QKV projection before the attention (model.py:289).
+
+    ``pair``: None (default) runs 256-row tiles over CTA pairs when x has more
+    than 128 rows and K >= 512 (not for :func:`linear_rope`); True / False force CTA pairs / one CTA per
+    128-row tile (the same result bit for bit: each output element sums over K
+    in the same order either way, ``tests/test_linear_gpu.py``).
+    ``grid_ctas`` caps the persistent CTAs (0: one per SM)."""
     out = _linear_out(x, w.shape[0], out, x.dtype)
-    return _linear_call(x, w, b, out, N.FDS_EPILOGUE_STORE, grid_ctas=grid_ctas)
+    return _linear_call(x, w, b, out, N.FDS_EPILOGUE_STORE, grid_ctas=grid_ctas, pair=pair)
 
 
 def linear_rope(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, cos: torch.Tensor,
                 sin: torch.Tensor, length: int, heads: int, out: torch.Tensor | None = None,
-                *, grid_ctas: int = 0) -> torch.Tensor:
+                *, grid_ctas: int = 0, pair: bool | None = None) -> torch.Tensor:
     """The DiT's QKV projection with RoPE in its epilogue: ``F.linear(x, w, b)``
     (rounded to x's dtype) followed by ``rope_split``'s rotation of the q and k
     column blocks (position = row % length), written as one [M, 3*heads*64]
@@ -524,11 +531,11 @@ def linear_rope(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, cos: t
     _rope_tables(cos, sin, min(length, x.shape[0]), x)
     out = _linear_out(x, n, out, x.dtype)
     return _linear_call(x, w, b, out, N.FDS_EPILOGUE_ROPE, cos=cos, sin=sin, seq_len=length,
-                        rope_cols=2 * heads * HEAD_DIM, grid_ctas=grid_ctas)
+                        rope_cols=2 * heads * HEAD_DIM, grid_ctas=grid_ctas, pair=pair)
 
 
 def accumulate(x: torch.Tensor, a: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None,
-               *, grid_ctas: int = 0) -> None:
+               *, grid_ctas: int = 0, pair: bool | None = None) -> None:
     """``x += a @ w.T`` in place: fp16 / bf16 operands, fp32 accumulation added
     straight into the fp32 residual x (no reduced-precision GEMM output, no
     separate add). Reference: ``accumulate`` (triton/src/fds_triton/model.py:
@@ -539,7 +546,7 @@ def accumulate(x: torch.Tensor, a: torch.Tensor, w: torch.Tensor, b: torch.Tenso
     _check(x.stride(1) == 1 and (x.shape[0] <= 1 or x.stride(0) % 4 == 0) and x.data_ptr() % 16 == 0,
            "x rows must be contiguous and 16-byte aligned")
     _check(x.shape == (a.shape[0], w.shape[0]), f"x must be [{a.shape[0]}, {w.shape[0]}], got {tuple(x.shape)}")
-    _linear_call(a, w, b, x, N.FDS_EPILOGUE_ACCUMULATE_F32, grid_ctas=grid_ctas)
+    _linear_call(a, w, b, x, N.FDS_EPILOGUE_ACCUMULATE_F32, grid_ctas=grid_ctas, pair=pair)
 
 
 def rope_tables(max_seq: int, device=None, dim: int = HEAD_DIM, base: float = 10000.0):

@@ -47,7 +47,7 @@
 extern "C" {
 #endif
 
-#define FDS_ABI_VERSION 3
+#define FDS_ABI_VERSION 4
 
 #if defined(_WIN32)
 #define FDS_API __declspec(dllexport)
@@ -232,6 +232,15 @@ FDS_API int fds_rope_attn_fwd_static(const FdsRopeArgs* args, void* stream);
 #define FDS_EPILOGUE_ROPE 1
 #define FDS_EPILOGUE_ACCUMULATE_F32 2
 
+/* FdsLinearArgs.cta_pair: AUTO uses 256-row tiles over clusters of two CTAs
+ * when m > 128, k >= 512 and the epilogue is not ROPE (each CTA loads its own 128 rows of a and half of
+ * the tile's w rows; one tensor-core operation spans both SMs), else 128-row
+ * tiles on one CTA each; SINGLE / PAIR force one of the two. Both give the
+ * same result bit for bit. */
+#define FDS_GEMM_AUTO 0
+#define FDS_GEMM_SINGLE 1
+#define FDS_GEMM_PAIR 2
+
 typedef struct FdsLinearArgs {
     const void* a;            /* device, dtype, [m, a_row_stride] */
     int64_t a_row_stride;     /* elements; multiple of 8, >= k */
@@ -253,6 +262,7 @@ typedef struct FdsLinearArgs {
     int32_t rope_cols;        /* FDS_EPILOGUE_ROPE: multiple of 64, <= n */
     int64_t timeout_ns;       /* bound on every in-kernel wait; <= 0 selects 2 s */
     int32_t grid_ctas;        /* persistent CTAs; 0 = one per SM */
+    int32_t cta_pair;         /* FDS_GEMM_*: tiles over CTA pairs (tcgen05 cta_group::2) or one CTA each */
 } FdsLinearArgs;
 
 FDS_API int fds_linear_fwd(const FdsLinearArgs* args, void* stream);

@@ -205,3 +205,74 @@ def test_accumulate_bf16_with_bias(cuda_device):
     F.check_status()
     delta = (a.double() @ w.double().t() + bias.double()).float()
     assert O.max_abs(x + delta, xd.cpu()) <= 1e-4 * float(delta.abs().max()) + 1e-5
+
+
+@pytest.mark.parametrize("m,k,n", [(6000, 1024, 3072), (6000, 1024, 1024), (129, 64, 128), (257, 128, 256),
+                                   (1, 64, 128)])
+def test_pair_and_single_cta_tiles(cuda_device, m, k, n):
+    """256-row tiles over CTA pairs (tcgen05 cta_group::2, the default for more
+    than 128 rows) and 128-row tiles on one CTA each, forced both ways, against
+    the fp32 product (m = 1 and 129: a pair whose second CTA has no valid row)."""
+    x, w, b, xd, wd, bd = _operands(m, k, n, seed=m + 3 * n)
+    ref = _ref(x, w, b)
+    for pair in (True, False):
+        _check_gemm(ref, F.linear(xd, wd, bd, pair=pair), torch.float16)
+    F.check_status()
+
+
+@pytest.mark.parametrize("grid_ctas", [2, 3, 4])
+def test_pair_tiles_on_few_ctas(cuda_device, grid_ctas):
+    """1-2 CTA pairs walking 24-48 tiles each (stage ring and accumulator
+    double buffer wrap many times across the pair's barriers)."""
+    x, w, b, xd, wd, bd = _operands(3000, 512, 2304, seed=grid_ctas)
+    _check_gemm(_ref(x, w, b), F.linear(xd, wd, bd, grid_ctas=grid_ctas, pair=True), torch.float16)
+    F.check_status()
+
+
+@pytest.mark.parametrize("pair", [True, False])
+def test_rope_and_accumulate_both_tilings(cuda_device, pair):
+    B, L, H = 2, 700, 12
+    hid = H * 64
+    x, w, b, xd, wd, bd = _operands(B * L, hid, 3 * hid, seed=51)
+    cos, sin = F.rope_tables(L, cuda_device)
+    got = F.linear_rope(xd, wd, bd, cos, sin, L, H, pair=pair).float().cpu()
+    exp = O.rope_split(_ref(x, w, b).half(), L, H, cos.cpu(), sin.cpu())
+    bound = 2 * ULP[torch.float16] * float(exp.abs().max()) + 1e-6
+    for part in range(3):
+        assert O.max_abs(exp[part], got[:, part * hid:(part + 1) * hid]) <= bound, part
+    m, k, n = B * L, 1024, 1024
+    g = torch.Generator().manual_seed(53)
+    r = torch.randn(m, n, generator=g)
+    a = torch.randn(m, k, generator=g).half()
+    wo = (torch.randn(n, k, generator=g) * 0.02).half()
+    rd = r.to(cuda_device)
+    F.accumulate(rd, a.to(cuda_device), wo.to(cuda_device), pair=pair)
+    F.check_status()
+    delta = (a.double() @ wo.double().t()).float()
+    assert O.max_abs(r + delta, rd.cpu()) <= 1e-4 * float(delta.abs().max()) + 1e-5
+
+
+@pytest.mark.parametrize("pair", [True, False])
+def test_rope_cols_not_a_multiple_of_the_tile_half(cuda_device, pair):
+    """fds_linear_fwd's RoPE epilogue rotates exactly the 64-column heads below
+    rope_cols, also when rope_cols (here 192 of 512) ends inside the 128-column
+    half of a tile one epilogue warp writes."""
+    from fastdialoguesidon_b200 import _native as N
+    from fastdialoguesidon_b200.kernels import _linear_call
+    L, n, k, rope_cols = 300, 512, 256, 192
+    x, w, b, xd, wd, bd = _operands(2 * L, k, n, seed=61)
+    cos, sin = F.rope_tables(L, cuda_device)
+    out = torch.empty(2 * L, n, dtype=torch.float16, device=cuda_device)
+    _linear_call(xd, wd, bd, out, N.FDS_EPILOGUE_ROPE, cos=cos, sin=sin, seq_len=L, rope_cols=rope_cols, pair=pair)
+    F.check_status()
+    y = _ref(x, w, b).half().float()                       # F.linear rounded to fp16
+    pos = torch.arange(2 * L) % L
+    c, s = cos.cpu()[pos], sin.cpu()[pos]                  # [rows, 64]
+    exp = y.clone()
+    for h in range(rope_cols // 64):
+        blk = y[:, 64 * h:64 * (h + 1)]
+        rot = torch.cat([-blk[:, 32:], blk[:, :32]], dim=1)
+        exp[:, 64 * h:64 * (h + 1)] = blk * c + rot * s
+    got = out.float().cpu()
+    bound = 2 * ULP[torch.float16] * float(exp.abs().max()) + 1e-6
+    assert O.max_abs(exp, got) <= bound  # a rotated head past rope_cols (or one left out) is far off
