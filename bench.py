@@ -73,9 +73,10 @@ def parse_args():
     ap.add_argument("--schedule", choices=("auto", "unit"), default="auto",
                     help="auto: the library picks whole units per CTA or the balanced (stream-K) grid; "
                          "unit: always one 256-row unit per CTA")
-    ap.add_argument("--case", choices=("enc1", "dit1", "qkv"), default=None,
-                    help="profiling case: W + K eager launches of one layer's attention (encoder or DiT) or of "
-                         "the encoder's QKV projection (qkv) at L=6000")
+    ap.add_argument("--case", choices=("enc1", "dit1", "qkv", "ropeqkv", "accum"), default=None,
+                    help="profiling case: W + K eager launches of one layer's attention (encoder or DiT), of the "
+                         "encoder's QKV projection (qkv), the DiT's QKV projection with RoPE (ropeqkv) or the "
+                         "encoder's out-projection into the fp32 residual (accum), at L=6000")
     ap.add_argument("--no-config3", action="store_true")
     ap.add_argument("--no-throughput", action="store_true")
     ap.add_argument("--no-linear", action="store_true")
@@ -497,8 +498,12 @@ def e2e_layer_leg(steps: int, warmup: int, device: torch.device, dist_on: bool) 
     window (6000 x 1024) is copied in from pinned host memory, each layer runs
     qkv = linear(x16, W_qkv, b) -> flexrel_attention -> accumulate(x, ctx, W_out)
     on the device (weights resident, random-init N(0, 0.02)), and x is copied
-    back. Work per window: the 13 attention layers plus their QKV and output
-    projections (13 x (147.5 + 37.7 + 12.6) GFLOP)."""
+    back. The 13 layers of a window are one CUDA graph (as the reference's
+    pipeline captures its model); windows alternate between two residual
+    buffers so that window k+1's copy in and window k-1's copy out overlap
+    window k's layers (copy-in / compute / copy-out streams). Work per window:
+    the 13 attention layers plus their QKV and output projections
+    (13 x (147.5 + 37.7 + 12.6) GFLOP)."""
     import fastdialoguesidon_b200 as F
 
     hid = ENC_HEADS * HEAD_DIM
@@ -508,20 +513,56 @@ def e2e_layer_leg(steps: int, warmup: int, device: torch.device, dist_on: bool) 
            (torch.randn(hid, hid, generator=g, device=device) * 0.02).half(),
            (torch.randn(73, HEAD_DIM, generator=g, device=device) * 0.02).half()) for _ in range(ENC_LAYERS)]
     host_x = torch.randn(L_WINDOW, hid, generator=torch.Generator().manual_seed(4001)).pin_memory()
-    host_out = torch.empty_like(host_x).pin_memory()
-    x = torch.empty(L_WINDOW, hid, device=device)
+    host_out = [torch.empty_like(host_x).pin_memory() for _ in range(2)]
+    xs = [torch.empty(L_WINDOW, hid, device=device) for _ in range(2)]
     x16 = torch.empty(L_WINDOW, hid, dtype=torch.float16, device=device)
     qkv = torch.empty(L_WINDOW, 3 * hid, dtype=torch.float16, device=device)
     ctx = torch.empty(L_WINDOW, hid, dtype=torch.float16, device=device)
+    comp = torch.cuda.Stream(device)
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
 
-    def step():
-        x.copy_(host_x, non_blocking=True)
+    def layers(x):
         for w_qkv, b_qkv, w_out, rel in ws:
             x16.copy_(x)
             F.linear(x16, w_qkv, b_qkv, out=qkv)
             F.flexrel_attention(qkv, 1, ENC_HEADS, rel, out=ctx)
             F.accumulate(x, ctx, w_out)
-        host_out.copy_(x, non_blocking=True)
+
+    comp.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(comp):
+        for b in range(2):  # eager warm-up (library state and workspaces are created outside capture)
+            xs[b].copy_(host_x)
+            layers(xs[b])
+    torch.cuda.synchronize(device)
+    graphs = []
+    for b in range(2):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=comp):
+            layers(xs[b])
+        graphs.append(gr)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_c = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    for b in range(2):
+        ev_c[b].record(comp)
+        ev_out[b].record(s_out)
+    k = [0]
+
+    def step():
+        b = k[0] & 1
+        k[0] += 1
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_out[b])  # the previous window in this buffer has been copied out
+            xs[b].copy_(host_x, non_blocking=True)
+            ev_in[b].record(s_in)
+        comp.wait_event(ev_in[b])
+        with torch.cuda.stream(comp):  # a graph replays on the current stream
+            graphs[b].replay()
+        ev_c[b].record(comp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_c[b])
+            host_out[b].copy_(xs[b], non_blocking=True)
+            ev_out[b].record(s_out)
 
     for _ in range(warmup):
         step()
@@ -530,12 +571,25 @@ def e2e_layer_leg(steps: int, warmup: int, device: torch.device, dist_on: bool) 
         torch.distributed.barrier()
     torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
+    e0.record(s_in)
     for _ in range(steps):
         step()
-    e1.record()
+    s_out.wait_stream(comp)
+    e1.record(s_out)
     torch.cuda.synchronize(device)
     F.check_status(device)
+    for gr in graphs:
+        del gr
+    graphs.clear()
+    # every window starts from the same x: the last one copied out must equal the
+    # same 13 layers run eagerly (same kernels, same order: bit for bit)
+    last = (k[0] - 1) & 1
+    with torch.cuda.stream(comp):
+        xs[last].copy_(host_x)
+        layers(xs[last])
+    torch.cuda.synchronize(device)
+    if not torch.equal(xs[last].cpu(), host_out[last]):
+        raise RuntimeError("e2e_layer: pipelined windows differ from the eager layers")
     nbytes = host_x.numel() * 4
     return {"ms": e0.elapsed_time(e1), "steps": steps, "h2d": nbytes, "d2h": nbytes}
 
@@ -772,8 +826,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                 "value": round(el_ms / (el["steps"] * world), 4), "unit": UNIT,
                 "h2d_bytes_per_step": el["h2d"], "d2h_bytes_per_step": el["d2h"],
                 "note": "the 13 attention layers with their projections on the device (linear -> "
-                        "flexrel_attention -> accumulate per layer, weights resident); only the fp32 residual "
-                        "of the window crosses the host link, in and out, each step"},
+                        "flexrel_attention -> accumulate per layer, weights resident, one CUDA graph per "
+                        "window); only the fp32 residual of the window crosses the host link, in and out, "
+                        "each step, overlapped with the neighbouring windows' layers"},
         }
         if dit:
             dsteps = dit[1]
@@ -838,6 +893,21 @@ def run_case(args) -> None:
         b = (torch.randn(3 * ENC_HEADS * HEAD_DIM, generator=gen, device=device) * 0.02).half()
         out = torch.empty(L_WINDOW, 3 * ENC_HEADS * HEAD_DIM, dtype=torch.float16, device=device)
         fn, flop = (lambda: F.linear(x, w, b, out=out)), 2.0 * L_WINDOW * x.shape[1] * w.shape[0]
+    elif args.case == "ropeqkv":
+        hid = DIT_HEADS * HEAD_DIM
+        x = torch.randn(L_WINDOW, hid, generator=gen, device=device).half()
+        w = (torch.randn(3 * hid, hid, generator=gen, device=device) * 0.02).half()
+        b = (torch.randn(3 * hid, generator=gen, device=device) * 0.02).half()
+        cos, sin = F.rope_tables(L_WINDOW, device)
+        out = torch.empty(L_WINDOW, 3 * hid, dtype=torch.float16, device=device)
+        fn = lambda: F.linear_rope(x, w, b, cos, sin, L_WINDOW, DIT_HEADS, out=out)  # noqa: E731
+        flop = 2.0 * L_WINDOW * hid * 3 * hid
+    elif args.case == "accum":
+        hid = ENC_HEADS * HEAD_DIM
+        a = torch.randn(L_WINDOW, hid, generator=gen, device=device).half()
+        w = (torch.randn(hid, hid, generator=gen, device=device) * 0.02).half()
+        x = torch.zeros(L_WINDOW, hid, device=device)
+        fn, flop = (lambda: F.accumulate(x, a, w)), 2.0 * L_WINDOW * hid * hid
     elif args.case == "enc1":
         qkv = (torch.randn(L_WINDOW, 3 * ENC_HEADS * HEAD_DIM, generator=gen, device=device) * 0.64).half()
         rel = (torch.randn(73, HEAD_DIM, generator=gen, device=device) * 0.02).half()
