@@ -592,11 +592,12 @@ __device__ __forceinline__ void mma_role(uint32_t sbase, uint32_t tmem, WaitCtl 
 // ---------------------------------------------------------------- softmax
 
 // Whether score pair c (of a tile's 64) is exponentiated by the FMA-pipe
-// polynomial instead of MUFU ex2: 3 pairs in 10 for the encoder, 2 in 10 for
-// the DiT (each the measured best of 10-35 % and of where in the 10 they sit).
+// polynomial instead of MUFU ex2: pairs 1, 4, 7 of every 10 in both kernels
+// (the measured best of 10-40 % and of where in the 10 they sit; the DiT's
+// best moved from 2 in 10 to 3 in 10 with the warpgroups' start offset).
 template <bool kRelBias>
 __device__ __forceinline__ constexpr bool poly_pair(int c) {
-    return kRelBias ? (c % 10 == 1 || c % 10 == 4 || c % 10 == 7) : (c % 10 == 2 || c % 10 == 7);
+    return c % 10 == 1 || c % 10 == 4 || c % 10 == 7;
 }
 
 // O *= alpha for this thread's row (32 lanes of a warp, 64 columns). Rare (the
