@@ -852,6 +852,27 @@ __device__ __forceinline__ void finish_part(const AttnParams& p, const float (&o
     if (lane == 0) *count = 0;
 }
 
+// The padded relative-bias row of query row i, T[m] = QR[clamp(m - 4 - R, 0, 72)]
+// (scaled to log2 units) for m in [0, 84), R = i mod 4, as 21 aligned 16-byte
+// stores: the row stride (84 words) keeps a quarter-warp's 16-byte accesses on
+// distinct banks, where one word per lane would hit each bank 4 times.
+template <int R>
+__device__ __forceinline__ void fill_qr_row(uint32_t qrow, const uint32_t (&a)[32], const uint32_t (&c2)[32],
+                                            const uint32_t (&d)[16], float sl) {
+#pragma unroll
+    for (int q = 0; q < kQrStride / 4; ++q) {
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            int k = 4 * q + e - 4 - R;
+            k = k < 0 ? 0 : (k > kNumPos - 1 ? kNumPos - 1 : k);
+            v[e] = __uint_as_float(k < 32 ? a[k] : (k < 64 ? c2[k - 32] : d[k - 64])) * sl;
+        }
+        st_shared_v4(qrow + 16u * q, make_int4(__float_as_int(v[0]), __float_as_int(v[1]), __float_as_int(v[2]),
+                                               __float_as_int(v[3])));
+    }
+}
+
 template <typename T, bool kRelBias, bool kQrGlobal>
 __device__ __forceinline__ void softmax_role(uint32_t sbase, uint32_t tmem, const AttnParams& p, WaitCtl ctl,
                                              int warp, int lane, int n_items) {
@@ -947,19 +968,12 @@ __device__ __forceinline__ void softmax_role(uint32_t sbase, uint32_t tmem, cons
             warp_arrive(rs.s_free, lane);  // the S columns may now receive the item's first S
             qr_left = __uint_as_float(a[0]) * sl;
             qr_right = __uint_as_float(d[kNumPos - 1 - 64]) * sl;
-            // padded table: QR[0] below, QR[72] above (written first), the row at
-            // offset 4 + (i & 3) over them
-            const uint32_t t = qrow + 4u * (4 + (i & 3));
-#pragma unroll
-            for (int m = 0; m < 7; ++m) st_shared_f32(qrow + 4u * m, qr_left);
-#pragma unroll
-            for (int m = kQrStride - 8; m < kQrStride; ++m) st_shared_f32(qrow + 4u * m, qr_right);
-#pragma unroll
-            for (int c = 0; c < 32; ++c) st_shared_f32(t + 4u * c, __uint_as_float(a[c]) * sl);
-#pragma unroll
-            for (int c = 0; c < 32; ++c) st_shared_f32(t + 4u * (32 + c), __uint_as_float(c2[c]) * sl);
-#pragma unroll
-            for (int c = 0; c < kNumPos - 64; ++c) st_shared_f32(t + 4u * (64 + c), __uint_as_float(d[c]) * sl);
+            switch (i & 3) {
+                case 0: fill_qr_row<0>(qrow, a, c2, d, sl); break;
+                case 1: fill_qr_row<1>(qrow, a, c2, d, sl); break;
+                case 2: fill_qr_row<2>(qrow, a, c2, d, sl); break;
+                default: fill_qr_row<3>(qrow, a, c2, d, sl); break;
+            }
         }
 
         // Tiles in key order: [.., jb0) every pair left-saturated (bias QR[i,0]),
