@@ -825,10 +825,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             "e2e_layer": {
                 "value": round(el_ms / (el["steps"] * world), 4), "unit": UNIT,
                 "h2d_bytes_per_step": el["h2d"], "d2h_bytes_per_step": el["d2h"],
+                "gpu_launches_per_window": 3 * ENC_LAYERS,
                 "note": "the 13 attention layers with their projections on the device (linear -> "
                         "flexrel_attention -> accumulate per layer, weights resident, one CUDA graph per "
                         "window); only the fp32 residual of the window crosses the host link, in and out, "
-                        "each step, overlapped with the neighbouring windows' layers"},
+                        "each step, overlapped with the neighbouring windows' layers; per layer this "
+                        "library's QKV GEMM, attention and out-projection GEMM plus torch's fp16 cast of x"},
         }
         if dit:
             dsteps = dit[1]
