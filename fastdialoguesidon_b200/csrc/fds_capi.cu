@@ -173,6 +173,21 @@ bool pdl_enabled() {
     return on;
 }
 
+// cudaFuncSetAttribute(kern, MaxDynamicSharedMemorySize, bytes) once per
+// kernel and device (it is per-device state, and a per-call driver round trip
+// otherwise); `done` is the kernel's own set of devices already configured.
+template <typename Kern>
+cudaError_t set_smem_once(Kern kern, int bytes, std::atomic<uint64_t>& done) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = dev >= 0 && dev < 64 ? (uint64_t{1} << dev) : 0;
+    if (bit != 0 && (done.load(std::memory_order_acquire) & bit) != 0) return cudaSuccess;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && bit != 0) done.fetch_or(bit, std::memory_order_release);
+    return e;
+}
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                        Args&&... args) {
@@ -262,7 +277,8 @@ template <typename T, bool kRelBias, bool kQrGlobal = false>
 int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mr,
                 fds::AttnParams p, int batch, const Workspace& ws, cudaStream_t stream) {
     auto kern = fds::attn_fwd_kernel<T, kRelBias, kQrGlobal>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fds::Smem::alloc);
+    static std::atomic<uint64_t> smem_set{0};
+    cudaError_t e = set_smem_once(kern, fds::Smem::alloc, smem_set);
     if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     p.row_blocks = (p.seq_len + fds::kRowsPerCta - 1) / fds::kRowsPerCta;
     const int64_t U = static_cast<int64_t>(batch) * p.heads * p.row_blocks;
@@ -359,7 +375,8 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
                 int grid, cudaStream_t stream) {
     auto kern = fds::gemm::gemm_kernel<T, BN, kEpi, kPair>;
     constexpr int smem = fds::gemm::Smem<BN, kPair>::alloc;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    static std::atomic<uint64_t> smem_set{0};
+    cudaError_t e = set_smem_once(kern, smem, smem_set);
     if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "cudaFuncSetAttribute(gemm): %s", cudaGetErrorString(e));
     const dim3 g(static_cast<unsigned>(grid)), b(fds::gemm::kThreads);
     e = kPair ? launch_pair(kern, g, b, smem, stream, ma, mb, mo, p) : launch_pdl(kern, g, b, smem, stream, ma, mb, mo, p);

@@ -36,6 +36,7 @@ to its window calls it once per window.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import math
 
@@ -57,14 +58,17 @@ class FdsError(AssertionError, RuntimeError):
 _DTYPES = {torch.float16: N.FDS_DTYPE_FP16, torch.bfloat16: N.FDS_DTYPE_BF16}
 _status_words: dict[int, torch.Tensor] = {}
 _status_mirrors: dict[int, torch.Tensor] = {}
+_mirror_views: dict = {}
 _workspaces: dict[tuple[int, int], torch.Tensor] = {}
 _spare_workspaces: dict[int, list[torch.Tensor]] = {}
 _SPARE_WORKSPACES = 2
 
 
-def _check(cond: bool, msg: str) -> None:
+def _check(cond: bool, msg) -> None:
+    """Raise FdsError(msg) unless cond; msg may be a zero-argument callable,
+    formatted only on failure (the checks run on every call)."""
     if not cond:
-        raise FdsError(msg)
+        raise FdsError(msg() if callable(msg) else msg)
 
 
 def _dev_index(device: torch.device) -> int:
@@ -96,12 +100,23 @@ def _status_mirror(device: torch.device) -> torch.Tensor:
     return m
 
 
+def _on_device(device: torch.device):
+    """``torch.cuda.device(device)``, or nothing when it is already current."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
+
+
 def _raise_if_timed_out(device: torch.device) -> None:
     """Raise (without a device sync) if a kernel on ``device`` reported a
     timeout that :func:`check_status` has not cleared yet."""
-    m = _status_mirrors.get(_dev_index(device))
+    idx = _dev_index(device)
+    m = _status_mirrors.get(idx)
     if m is not None:
-        bits = int(m[0])
+        view = _mirror_views.get(idx)
+        if view is None or view[0] is not m:  # the same pinned words, read without torch indexing
+            view = _mirror_views[idx] = (m, m.numpy())
+        bits = int(view[1][0])
         if bits:
             raise FdsError(f"an earlier FDS kernel on cuda:{_dev_index(device)} reported a bounded-wait "
                            f"timeout (status bits 0x{bits:x}); call check_status() to clear it")
@@ -132,7 +147,16 @@ def check_status(device: torch.device | int | None = None, clear: bool = True) -
 
 
 def _stream_ptr(device: torch.device) -> int:
+    """The current stream of ``device`` as a raw ``cudaStream_t`` value."""
+    if _raw_stream is not None:
+        return _raw_stream(_dev_index(device))
     return torch.cuda.current_stream(device).cuda_stream
+
+
+# torch's own accessor for the current raw stream (what its compiled kernels
+# launch on), much cheaper than building a Stream object; the public call
+# otherwise
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
 
 
 def _workspace(device: torch.device, lib) -> torch.Tensor | None:
@@ -176,12 +200,12 @@ def _schedule(device: torch.device, lib, balanced: bool, grid_ctas: int) -> dict
 
 
 def _rows_operand(t: torch.Tensor, name: str) -> None:
-    _check(isinstance(t, torch.Tensor), f"{name} must be a torch.Tensor")
-    _check(t.dim() == 2, f"{name} must be 2-D [rows, columns], got {tuple(t.shape)}")
-    _check(t.dtype in _DTYPES, f"{name} must be float16 or bfloat16, got {t.dtype}")
-    _check(t.stride(1) == 1, f"{name} columns must be contiguous (stride(1) == 1)")
-    _check(t.shape[0] <= 1 or t.stride(0) % 8 == 0, f"{name} row stride must be a multiple of 8 elements")
-    _check(t.data_ptr() % 16 == 0, f"{name} must be 16-byte aligned")
+    _check(isinstance(t, torch.Tensor), lambda: f"{name} must be a torch.Tensor")
+    _check(t.dim() == 2, lambda: f"{name} must be 2-D [rows, columns], got {tuple(t.shape)}")
+    _check(t.dtype in _DTYPES, lambda: f"{name} must be float16 or bfloat16, got {t.dtype}")
+    _check(t.stride(1) == 1, lambda: f"{name} columns must be contiguous (stride(1) == 1)")
+    _check(t.shape[0] <= 1 or t.stride(0) % 8 == 0, lambda: f"{name} row stride must be a multiple of 8 elements")
+    _check(t.data_ptr() % 16 == 0, lambda: f"{name} must be 16-byte aligned")
 
 
 def _on_cuda(*tensors: torch.Tensor) -> None:
@@ -216,34 +240,34 @@ def flexrel_attention(qkv: torch.Tensor, batch: int, heads: int, rel: torch.Tens
     _rows_operand(qkv, "qkv")
     rows, width = qkv.shape
     _check(batch >= 1 and heads >= 1, "batch and heads must be >= 1")
-    _check(width % 3 == 0, f"qkv width {width} is not 3 * hidden")
+    _check(width % 3 == 0, lambda: f"qkv width {width} is not 3 * hidden")
     hidden = width // 3
-    _check(hidden % heads == 0, f"hidden {hidden} not divisible by heads {heads}")
+    _check(hidden % heads == 0, lambda: f"hidden {hidden} not divisible by heads {heads}")
     dim = hidden // heads
-    _check(dim == HEAD_DIM, f"head_dim must be 64, got {dim}")
-    _check(rows % batch == 0 and rows > 0, f"rows {rows} not a positive multiple of batch {batch}")
+    _check(dim == HEAD_DIM, lambda: f"head_dim must be 64, got {dim}")
+    _check(rows % batch == 0 and rows > 0, lambda: f"rows {rows} not a positive multiple of batch {batch}")
     length = rows // batch
     _check(isinstance(rel, torch.Tensor) and rel.shape == (NUM_POS, dim) and rel.is_contiguous(),
-           f"rel must be a contiguous [{NUM_POS}, {dim}] tensor")
+           lambda: f"rel must be a contiguous [{NUM_POS}, {dim}] tensor")
     _check(rel.dtype == qkv.dtype and rel.device == qkv.device, "rel must match qkv's dtype and device")
     _check(rel.data_ptr() % 16 == 0, "rel must be 16-byte aligned")
     if out is None:
         out = torch.empty(rows, hidden, device=qkv.device, dtype=qkv.dtype)
     else:
         _rows_operand(out, "out")
-        _check(out.shape == (rows, hidden), f"out must be [{rows}, {hidden}], got {tuple(out.shape)}")
+        _check(out.shape == (rows, hidden), lambda: f"out must be [{rows}, {hidden}], got {tuple(out.shape)}")
         _check(out.dtype == qkv.dtype and out.device == qkv.device, "out must match qkv's dtype and device")
     kv_ptr = None
     if kv_len is not None:
         _check(isinstance(kv_len, torch.Tensor) and kv_len.dtype == torch.int32
                and kv_len.shape == (batch,) and kv_len.is_contiguous() and kv_len.device == qkv.device,
-               f"kv_len must be a contiguous int32 CUDA tensor of shape [{batch}] on qkv's device")
+               lambda: f"kv_len must be a contiguous int32 CUDA tensor of shape [{batch}] on qkv's device")
         kv_ptr = kv_len.data_ptr()
     _on_cuda(qkv, rel, out)
     dev = qkv.device
     _raise_if_timed_out(dev)
     lib = N.load()
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         args = N.FdsFlexRelArgs(
             qkv=qkv.data_ptr(), qkv_row_stride=qkv.stride(0) if rows > 1 else width,
             rel=rel.data_ptr(), out=out.data_ptr(),
@@ -271,35 +295,35 @@ def flexrel_attention_qr(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, qr: 
     flexrel_triton.py:749-780). ``kv_len`` as in :func:`flexrel_attention`."""
     for name, t in (("q", q), ("k", k), ("v", v), ("qr", qr)):
         _check(isinstance(t, torch.Tensor) and t.dim() == 4 and t.is_contiguous(),
-               f"{name} must be a contiguous 4-D tensor")
+               lambda: f"{name} must be a contiguous 4-D tensor")
         _check(t.dtype in _DTYPES and t.dtype == q.dtype and t.device == q.device,
-               f"{name} must be float16 / bfloat16 like q, on q's device")
+               lambda: f"{name} must be float16 / bfloat16 like q, on q's device")
     _check(q.shape == k.shape == v.shape, "q, k and v must have the same shape")
     if heads_last:
         batch, length, heads, dim = q.shape
-        _check(qr.shape == (batch, length, heads, NUM_POS), f"qr must be [{batch}, {length}, {heads}, {NUM_POS}]")
+        _check(qr.shape == (batch, length, heads, NUM_POS), lambda: f"qr must be [{batch}, {length}, {heads}, {NUM_POS}]")
     else:
         batch, heads, length, dim = q.shape
-        _check(qr.shape == (batch, heads, length, NUM_POS), f"qr must be [{batch}, {heads}, {length}, {NUM_POS}]")
-    _check(dim == HEAD_DIM, f"head_dim must be 64, got {dim}")
+        _check(qr.shape == (batch, heads, length, NUM_POS), lambda: f"qr must be [{batch}, {heads}, {length}, {NUM_POS}]")
+    _check(dim == HEAD_DIM, lambda: f"head_dim must be 64, got {dim}")
     for name, t in (("q", q), ("k", k), ("v", v)):
-        _check(t.data_ptr() % 16 == 0, f"{name} must be 16-byte aligned")
+        _check(t.data_ptr() % 16 == 0, lambda: f"{name} must be 16-byte aligned")
     if out is None:
         out = torch.empty_like(q)
     else:
         _check(out.shape == q.shape and out.dtype == q.dtype and out.device == q.device and out.is_contiguous()
-               and out.data_ptr() % 16 == 0, f"out must be a contiguous {tuple(q.shape)} {q.dtype} tensor")
+               and out.data_ptr() % 16 == 0, lambda: f"out must be a contiguous {tuple(q.shape)} {q.dtype} tensor")
     kv_ptr = None
     if kv_len is not None:
         _check(isinstance(kv_len, torch.Tensor) and kv_len.dtype == torch.int32
                and kv_len.shape == (batch,) and kv_len.is_contiguous() and kv_len.device == q.device,
-               f"kv_len must be a contiguous int32 CUDA tensor of shape [{batch}] on q's device")
+               lambda: f"kv_len must be a contiguous int32 CUDA tensor of shape [{batch}] on q's device")
         kv_ptr = kv_len.data_ptr()
     _on_cuda(q, k, v, qr, out)
     dev = q.device
     _raise_if_timed_out(dev)
     lib = N.load()
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         args = N.FdsFlexRelQrArgs(
             q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), qr=qr.data_ptr(), out=out.data_ptr(),
             kv_len=kv_ptr, status=_status(dev).data_ptr(), status_host=_status_mirror(dev).data_ptr(),
@@ -332,7 +356,7 @@ def cudnn_attention_available(device=None) -> bool:
 def encoder_attention(qkv, batch, heads, rel, impl: str = "split", kv_len=None):
     """Reference ``kernels.py:674``; ``impl`` ("split" / "fused" / "auto") is
     accepted and ignored: there is a single kernel."""
-    _check(impl in ("split", "fused", "auto"), f"unknown impl {impl!r}")
+    _check(impl in ("split", "fused", "auto"), lambda: f"unknown impl {impl!r}")
     return flexrel_attention(qkv, batch, heads, rel, kv_len=kv_len)
 
 
@@ -341,7 +365,7 @@ def _rope_tables(cos: torch.Tensor, sin: torch.Tensor, length: int, ref: torch.T
         _check(isinstance(t, torch.Tensor) and t.dtype == torch.float32 and t.dim() == 2
                and t.shape[1] == HEAD_DIM and t.shape[0] >= length and t.is_contiguous()
                and t.device == ref.device and t.data_ptr() % 16 == 0,
-               f"{name} must be a contiguous fp32 [>= {length}, 64] table on {ref.device}")
+               lambda: f"{name} must be a contiguous fp32 [>= {length}, 64] table on {ref.device}")
 
 
 def rope_split(qkv: torch.Tensor, length: int, heads: int, cos: torch.Tensor,
@@ -384,7 +408,7 @@ def rope_attention(qkv: torch.Tensor, batch: int, heads: int, cos: torch.Tensor,
     _check(width % 3 == 0, "qkv width is not 3 * hidden")
     hid = width // 3
     _check(hid % heads == 0 and hid // heads == HEAD_DIM, "head_dim must be 64")
-    _check(rows % batch == 0 and rows > 0, f"rows {rows} not a positive multiple of batch {batch}")
+    _check(rows % batch == 0 and rows > 0, lambda: f"rows {rows} not a positive multiple of batch {batch}")
     length = rows // batch
     _rope_tables(cos, sin, length, qkv)
     if out is None:
@@ -392,18 +416,18 @@ def rope_attention(qkv: torch.Tensor, batch: int, heads: int, cos: torch.Tensor,
     else:
         _rows_operand(out, "out")
         _check(out.shape == (rows, hid) and out.dtype == qkv.dtype and out.device == qkv.device,
-               f"out must be a [{rows}, {hid}] {qkv.dtype} tensor on {qkv.device}")
+               lambda: f"out must be a [{rows}, {hid}] {qkv.dtype} tensor on {qkv.device}")
     if scratch is None:
         scratch = torch.empty(rows, 2 * hid, device=qkv.device, dtype=qkv.dtype)
     else:
         _check(scratch.shape == (rows, 2 * hid) and scratch.is_contiguous() and scratch.dtype == qkv.dtype
                and scratch.device == qkv.device and scratch.data_ptr() % 16 == 0,
-               f"scratch must be a contiguous [{rows}, {2 * hid}] {qkv.dtype} tensor on {qkv.device}")
+               lambda: f"scratch must be a contiguous [{rows}, {2 * hid}] {qkv.dtype} tensor on {qkv.device}")
     _on_cuda(qkv, cos, sin, out, scratch)
     dev = qkv.device
     _raise_if_timed_out(dev)
     lib = N.load()
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         args = N.FdsRopeArgs(
             qkv=qkv.data_ptr(), qkv_row_stride=qkv.stride(0) if rows > 1 else width,
             cos=cos.data_ptr(), sin=sin.data_ptr(), qk_scratch=scratch.data_ptr(), out=out.data_ptr(),
@@ -430,19 +454,19 @@ def rotated_attention(qkv: torch.Tensor, batch: int, heads: int, out: torch.Tens
     _check(width % 3 == 0, "qkv width is not 3 * hidden")
     hid = width // 3
     _check(hid % heads == 0 and hid // heads == HEAD_DIM, "head_dim must be 64")
-    _check(rows % batch == 0 and rows > 0, f"rows {rows} not a positive multiple of batch {batch}")
+    _check(rows % batch == 0 and rows > 0, lambda: f"rows {rows} not a positive multiple of batch {batch}")
     length = rows // batch
     if out is None:
         out = torch.empty(rows, hid, device=qkv.device, dtype=qkv.dtype)
     else:
         _rows_operand(out, "out")
         _check(out.shape == (rows, hid) and out.dtype == qkv.dtype and out.device == qkv.device,
-               f"out must be a [{rows}, {hid}] {qkv.dtype} tensor on {qkv.device}")
+               lambda: f"out must be a [{rows}, {hid}] {qkv.dtype} tensor on {qkv.device}")
     _on_cuda(qkv, out)
     dev = qkv.device
     _raise_if_timed_out(dev)
     lib = N.load()
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         args = N.FdsRopeArgs(
             qkv=qkv.data_ptr(), qkv_row_stride=qkv.stride(0) if rows > 1 else width,
             cos=None, sin=None, qk_scratch=None, out=out.data_ptr(),
@@ -464,19 +488,19 @@ def _linear_call(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, ou
     _rows_operand(w, "w")
     m, k = x.shape
     n, kw = w.shape
-    _check(kw == k, f"w is [{n}, {kw}] but x has {k} columns")
+    _check(kw == k, lambda: f"w is [{n}, {kw}] but x has {k} columns")
     _check(w.dtype == x.dtype and w.device == x.device, "w must match x's dtype and device")
-    _check(k % 64 == 0, f"in_features must be a multiple of 64 (got {k})")
-    _check(n % 128 == 0, f"out_features must be a multiple of 128 (got {n})")
+    _check(k % 64 == 0, lambda: f"in_features must be a multiple of 64 (got {k})")
+    _check(n % 128 == 0, lambda: f"out_features must be a multiple of 128 (got {n})")
     if bias is not None:
         _check(isinstance(bias, torch.Tensor) and bias.shape == (n,) and bias.is_contiguous()
                and bias.dtype == x.dtype and bias.device == x.device and bias.data_ptr() % 16 == 0,
-               f"bias must be a contiguous [{n}] {x.dtype} tensor on {x.device}")
+               lambda: f"bias must be a contiguous [{n}] {x.dtype} tensor on {x.device}")
     _on_cuda(x, w, out)
     dev = x.device
     _raise_if_timed_out(dev)
     lib = N.load()
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         args = N.FdsLinearArgs(
             a=x.data_ptr(), a_row_stride=x.stride(0) if m > 1 else k, w=w.data_ptr(),
             w_row_stride=w.stride(0) if n > 1 else k, bias=None if bias is None else bias.data_ptr(),
@@ -497,7 +521,7 @@ def _linear_out(x: torch.Tensor, n: int, out: torch.Tensor | None, dtype) -> tor
         return torch.empty(m, n, device=x.device, dtype=dtype)
     _rows_operand(out, "out") if dtype != torch.float32 else None
     _check(out.shape == (m, n) and out.dtype == dtype and out.device == x.device and out.stride(1) == 1,
-           f"out must be a [{m}, {n}] {dtype} tensor on {x.device} with contiguous rows")
+           lambda: f"out must be a [{m}, {n}] {dtype} tensor on {x.device} with contiguous rows")
     return out
 
 
@@ -526,7 +550,7 @@ def linear_rope(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, cos: t
     tensor that :func:`rotated_attention` reads directly. Replaces
     triton/src/fds_triton/model.py:318-319 (linear + K.rope_split)."""
     n = w.shape[0]
-    _check(n == 3 * heads * HEAD_DIM, f"w must have 3*heads*64 = {3 * heads * HEAD_DIM} rows (got {n})")
+    _check(n == 3 * heads * HEAD_DIM, lambda: f"w must have 3*heads*64 = {3 * heads * HEAD_DIM} rows (got {n})")
     _check(length >= 1, "length must be >= 1")
     _rope_tables(cos, sin, min(length, x.shape[0]), x)
     out = _linear_out(x, n, out, x.dtype)
@@ -545,7 +569,7 @@ def accumulate(x: torch.Tensor, a: torch.Tensor, w: torch.Tensor, b: torch.Tenso
            "x must be a 2-D fp32 tensor (the residual stream)")
     _check(x.stride(1) == 1 and (x.shape[0] <= 1 or x.stride(0) % 4 == 0) and x.data_ptr() % 16 == 0,
            "x rows must be contiguous and 16-byte aligned")
-    _check(x.shape == (a.shape[0], w.shape[0]), f"x must be [{a.shape[0]}, {w.shape[0]}], got {tuple(x.shape)}")
+    _check(x.shape == (a.shape[0], w.shape[0]), lambda: f"x must be [{a.shape[0]}, {w.shape[0]}], got {tuple(x.shape)}")
     _linear_call(a, w, b, x, N.FDS_EPILOGUE_ACCUMULATE_F32, grid_ctas=grid_ctas, pair=pair)
 
 

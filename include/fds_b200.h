@@ -37,6 +37,10 @@
  * any time, e.g. before its next call, without synchronising the device. The
  * store is plain (not atomic across the PCIe link): concurrent failures may
  * leave only some of their bits, but never zero.
+ *
+ * Per-device state the library caches on first use (kernel shared-memory
+ * limits, the co-resident CTA-pair count, the static scratch address) does
+ * not survive cudaDeviceReset of that device.
  */
 #ifndef FDS_B200_H
 #define FDS_B200_H
