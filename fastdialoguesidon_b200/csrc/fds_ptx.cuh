@@ -491,8 +491,8 @@ __device__ __forceinline__ float fma_sat(float a, float b, float c) {
 // kb = (add - kPolyLo) / kPolySpan; a saturating FMA maps s to
 // y = clamp((x - kPolyLo) / kPolySpan, 0, 1), i.e. x is clamped to
 // [kPolyLo, kPolyLo + kPolySpan] = [-126, 66], for every input including
-// -inf and values far above the softmax's range (2^66 is far beyond what the
-// callers accept, so such a tile is always redone with its exact maximum).
+// -inf and values far above the softmax's range (the softmax only passes
+// x <= its lazy-rescale threshold, 8; the clamp keeps any other input finite).
 // Then x = j + f with j = round(x) from the 1.5 * 2^23 shifter
 // (t = y * span + (C + lo) holds j in its low mantissa bits, exactly),
 // f = y * span + (C + lo - t) in [-1/2, 1/2] with a single rounding;

@@ -109,7 +109,7 @@ def test_exp2_polynomial_error_bound():
     fp32 with the same steps (each FMA with a single rounding), stays within
     1e-4 relative error of exp2 over the softmax's working range, gives tiny
     non-negative values below its clamp (-inf included) and huge finite values
-    above it (so that the speculative softmax always redoes such a tile)."""
+    above it (no inf or NaN whatever the input)."""
     src = open(__import__("pathlib").Path(__file__).resolve().parents[1] /
                "fastdialoguesidon_b200" / "csrc" / "fds_ptx.cuh").read()
     import re
