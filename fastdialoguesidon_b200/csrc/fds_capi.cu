@@ -161,6 +161,23 @@ int make_out_map(CUtensorMap* map, void* base, bool f32, int dtype, int64_t cols
     return FDS_OK;
 }
 
+// A RoPE table (fp32 [>= seq_len, 64], rows of 256 bytes) for the linear
+// layers' RoPE epilogue: boxes of 128 rows x the first 32 columns (the table is
+// cat([f, f]): the second half repeats them), 128-byte swizzle.
+int make_rope_table_map(CUtensorMap* map, const float* base, int64_t seq_len) {
+    EncodeTiledFn enc = encode_fn();
+    if (enc == nullptr) return fail(FDS_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled unavailable from the driver");
+    const cuuint64_t dims[2] = {64, static_cast<cuuint64_t>(seq_len)};
+    const cuuint64_t strides[1] = {64 * 4};
+    const cuuint32_t box[2] = {32, static_cast<cuuint32_t>(fds::gemm::kBM)};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(FDS_ERR_TENSOR_MAP, "cuTensorMapEncodeTiled(rope table) failed (%d)", static_cast<int>(r));
+    return FDS_OK;
+}
+
 // Kernels are launched with programmatic stream serialization: a launch may
 // start its CTAs while the previous kernel in the stream drains, and waits in
 // the kernel (griddepcontrol.wait) before touching memory. FDS_PDL=0 in the
@@ -370,39 +387,44 @@ cudaError_t launch_pair(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sm
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
+// The linear layers' tensor maps: A, W, the output, and the RoPE epilogue's
+// cos / sin tables (copies of the output map for the other epilogues).
+struct GemmMaps {
+    CUtensorMap a, b, out, cos, sin;
+};
+
 template <typename T, int BN, int kEpi, bool kPair>
-int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, const fds::gemm::Params& p,
-                int grid, cudaStream_t stream) {
+int launch_gemm(const GemmMaps& m, const fds::gemm::Params& p, int grid, cudaStream_t stream) {
     auto kern = fds::gemm::gemm_kernel<T, BN, kEpi, kPair>;
-    constexpr int smem = fds::gemm::Smem<BN, kPair>::alloc;
+    constexpr int smem = fds::gemm::Smem<BN, kPair, kEpi == fds::gemm::kRope>::alloc;
     static std::atomic<uint64_t> smem_set{0};
     cudaError_t e = set_smem_once(kern, smem, smem_set);
     if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "cudaFuncSetAttribute(gemm): %s", cudaGetErrorString(e));
     const dim3 g(static_cast<unsigned>(grid)), b(fds::gemm::kThreads);
-    e = kPair ? launch_pair(kern, g, b, smem, stream, ma, mb, mo, p) : launch_pdl(kern, g, b, smem, stream, ma, mb, mo, p);
+    e = kPair ? launch_pair(kern, g, b, smem, stream, m.a, m.b, m.out, m.cos, m.sin, p)
+              : launch_pdl(kern, g, b, smem, stream, m.a, m.b, m.out, m.cos, m.sin, p);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return fail(FDS_ERR_CUDA, "linear launch: %s", cudaGetErrorString(e));
     return FDS_OK;
 }
 
 template <typename T, int BN, bool kPair>
-int launch_gemm_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo,
-                    const fds::gemm::Params& p, int grid, cudaStream_t stream) {
+int launch_gemm_epi(int epi, const GemmMaps& m, const fds::gemm::Params& p, int grid, cudaStream_t stream) {
     switch (epi) {
-        case FDS_EPILOGUE_STORE: return launch_gemm<T, BN, fds::gemm::kStore, kPair>(ma, mb, mo, p, grid, stream);
-        case FDS_EPILOGUE_ROPE: return launch_gemm<T, BN, fds::gemm::kRope, kPair>(ma, mb, mo, p, grid, stream);
-        default: return launch_gemm<T, BN, fds::gemm::kAccum, kPair>(ma, mb, mo, p, grid, stream);
+        case FDS_EPILOGUE_STORE: return launch_gemm<T, BN, fds::gemm::kStore, kPair>(m, p, grid, stream);
+        case FDS_EPILOGUE_ROPE: return launch_gemm<T, BN, fds::gemm::kRope, kPair>(m, p, grid, stream);
+        default: return launch_gemm<T, BN, fds::gemm::kAccum, kPair>(m, p, grid, stream);
     }
 }
 
 template <typename T>
-int launch_gemm_shape(int bn, bool pair, int epi, const CUtensorMap& ma, const CUtensorMap& mb,
-                      const CUtensorMap& mo, const fds::gemm::Params& p, int grid, cudaStream_t stream) {
+int launch_gemm_shape(int bn, bool pair, int epi, const GemmMaps& m, const fds::gemm::Params& p, int grid,
+                      cudaStream_t stream) {
     if (pair)
-        return bn == 256 ? launch_gemm_epi<T, 256, true>(epi, ma, mb, mo, p, grid, stream)
-                         : launch_gemm_epi<T, 128, true>(epi, ma, mb, mo, p, grid, stream);
-    return bn == 256 ? launch_gemm_epi<T, 256, false>(epi, ma, mb, mo, p, grid, stream)
-                     : launch_gemm_epi<T, 128, false>(epi, ma, mb, mo, p, grid, stream);
+        return bn == 256 ? launch_gemm_epi<T, 256, true>(epi, m, p, grid, stream)
+                         : launch_gemm_epi<T, 128, true>(epi, m, p, grid, stream);
+    return bn == 256 ? launch_gemm_epi<T, 256, false>(epi, m, p, grid, stream)
+                     : launch_gemm_epi<T, 128, false>(epi, m, p, grid, stream);
 }
 
 // How many CTA pairs of the pair GEMM can be resident at once on the current
@@ -698,12 +720,9 @@ int fds_linear_fwd(const FdsLinearArgs* a, void* stream) {
     int64_t ctas = a->grid_ctas > 0 ? a->grid_ctas : (sms > 0 ? sms : 148);
     // CTA pairs (256-row tiles) unless asked otherwise, there is only one
     // 128-row tile of output rows, k is short (below 512 the pair's extra set-up
-    // and cluster barriers are not repaid), the epilogue is RoPE (it, not the
-    // k-loop, bounds the kernel, and a pair waits for the slower of its two
-    // CTAs' epilogues) -- both measured at m = 6000 -- or no pair can be placed
-    bool pair = a->cta_pair == FDS_GEMM_PAIR ||
-                (a->cta_pair == FDS_GEMM_AUTO && a->m > fds::gemm::kBM && a->k >= 512 &&
-                 a->epilogue != FDS_EPILOGUE_ROPE);
+    // and cluster barriers are not repaid: measured at m = 6000), or no pair can
+    // be placed
+    bool pair = a->cta_pair == FDS_GEMM_PAIR || (a->cta_pair == FDS_GEMM_AUTO && a->m > fds::gemm::kBM && a->k >= 512);
     if (pair) {
         const int64_t pairs = std::min<int64_t>(ctas / 2, max_pairs());
         if (pairs < 1) {
@@ -720,11 +739,19 @@ int fds_linear_fwd(const FdsLinearArgs* a, void* stream) {
     const int64_t tiles = static_cast<int64_t>((a->m + tile_m - 1) / tile_m) * (a->n / bn);
     if (tiles > 0x7fffffffLL) return fail(FDS_ERR_INVALID_ARGUMENT, "too many tiles");
 
-    CUtensorMap ma, mb, mo;
-    if ((rc = make_matrix_map(&ma, a->a, a->dtype, a->k, a->m, a->a_row_stride, fds::gemm::kBM)) != FDS_OK) return rc;
-    if ((rc = make_matrix_map(&mb, a->w, a->dtype, a->k, a->n, a->w_row_stride, pair ? bn / 2 : bn)) != FDS_OK)
+    GemmMaps maps;
+    if ((rc = make_matrix_map(&maps.a, a->a, a->dtype, a->k, a->m, a->a_row_stride, fds::gemm::kBM)) != FDS_OK)
         return rc;
-    if ((rc = make_out_map(&mo, a->out, f32_out, a->dtype, a->n, a->m, a->out_row_stride)) != FDS_OK) return rc;
+    if ((rc = make_matrix_map(&maps.b, a->w, a->dtype, a->k, a->n, a->w_row_stride, pair ? bn / 2 : bn)) != FDS_OK)
+        return rc;
+    if ((rc = make_out_map(&maps.out, a->out, f32_out, a->dtype, a->n, a->m, a->out_row_stride)) != FDS_OK) return rc;
+    if (a->epilogue == FDS_EPILOGUE_ROPE) {
+        if ((rc = make_rope_table_map(&maps.cos, a->cos, a->seq_len)) != FDS_OK) return rc;
+        if ((rc = make_rope_table_map(&maps.sin, a->sin, a->seq_len)) != FDS_OK) return rc;
+    } else {
+        maps.cos = maps.out;
+        maps.sin = maps.out;
+    }
     fds::gemm::Params p{};
     p.bias = a->bias;
     p.cos_t = a->cos;
@@ -741,8 +768,8 @@ int fds_linear_fwd(const FdsLinearArgs* a, void* stream) {
     p.tiles = static_cast<int32_t>(tiles);
     const int grid = static_cast<int>((tiles < units ? tiles : units) * (pair ? 2 : 1));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    rc = a->dtype == FDS_DTYPE_FP16 ? launch_gemm_shape<__half>(bn, pair, a->epilogue, ma, mb, mo, p, grid, s)
-                                    : launch_gemm_shape<__nv_bfloat16>(bn, pair, a->epilogue, ma, mb, mo, p, grid, s);
+    rc = a->dtype == FDS_DTYPE_FP16 ? launch_gemm_shape<__half>(bn, pair, a->epilogue, maps, p, grid, s)
+                                    : launch_gemm_shape<__nv_bfloat16>(bn, pair, a->epilogue, maps, p, grid, s);
     return rc == FDS_OK ? ok() : rc;
 }
 

@@ -54,31 +54,37 @@ enum Epi : int { kStore = 0, kRope = 1, kAccum = 2 };
 // The ring is as deep as 192 KB allows (a stage is a 128 x 64 A tile and this
 // CTA's W rows): the copies in flight have to cover the L2 / HBM latency of a
 // stage while the tensor cores eat one stage per 256 / 512 cycles.
-template <int BN, bool kPair>
+// kCs: the RoPE epilogue's cos / sin rows of the tile (128 rows x 32 fp32 of
+// each table, 128-byte swizzle) take 32 KB from the ring.
+template <int BN, bool kPair, bool kCs = false>
 struct Smem {
     static constexpr int kBNc = kPair ? BN / 2 : BN;  // W rows this CTA loads per tile
     static constexpr int a_bytes = kBM * kBK * 2;
     static constexpr int b_bytes = kBNc * kBK * 2;
-    static constexpr int kStages = (192 * 1024) / (a_bytes + b_bytes);
+    static constexpr int kCsBytes = kCs ? 2 * kBM * 128 : 0;
+    static constexpr int kStages = (192 * 1024 - kCsBytes) / (a_bytes + b_bytes);
     static constexpr int a = 0;
     static constexpr int b = a + kStages * a_bytes;
     // one staging box per epilogue warp: 32 rows x 128 bytes, 1024-aligned (the
     // 128-byte swizzle repeats every 8 rows)
     static constexpr int kStgBytes = 32 * 128;
     static constexpr int stg = b + kStages * b_bytes;
-    static constexpr int bars = stg + kEpiWarps * kStgBytes;
+    static constexpr int cs = stg + kEpiWarps * kStgBytes;  // cos rows, then sin rows
+    static constexpr int bars = cs + kCsBytes;
     static constexpr int kFull = 0;                 // [stage] A and W tiles landed (a pair: both CTAs', on the even CTA)
     static constexpr int kEmpty = kFull + kStages;  // [stage] MMAs done with the stage
     static constexpr int kAccFull = kEmpty + kStages;    // [buffer] tile's accumulator complete
     static constexpr int kAccEmpty = kAccFull + 2;       // [buffer] epilogue read it out (a pair: both CTAs', on the even CTA)
     static constexpr int kDrain = kAccEmpty + 2;
-    static constexpr int kNumBars = kDrain + 1;
+    static constexpr int kCsFull = kDrain + 1;   // the tile's cos / sin rows landed (or are not needed)
+    static constexpr int kCsEmpty = kCsFull + 1; // every epilogue warp has its rows in registers
+    static constexpr int kNumBars = kCsEmpty + 1;
     // misc block, same offsets as the attention kernel's (the bounded waits read
     // it): +0 TMEM base, +4 abort flag, +8 status pointer, +16 timeout, +32 mirror
     static constexpr int misc = bars + kNumBars * 8;
     static constexpr int total = misc + 48;
     static constexpr int alloc = total + 1024;
-    static_assert(stg % 1024 == 0 && alloc <= 227 * 1024, "shared-memory layout");
+    static_assert(stg % 1024 == 0 && cs % 1024 == 0 && alloc <= 227 * 1024, "shared-memory layout");
 };
 
 struct Params {
@@ -145,8 +151,9 @@ __device__ __forceinline__ void stage_row(uint32_t srow, int lane, const uint32_
 template <typename T, int BN, int kEpi, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                const __grid_constant__ CUtensorMap map_out, const Params p) {
-    using S = Smem<BN, kPair>;
+                const __grid_constant__ CUtensorMap map_out, const __grid_constant__ CUtensorMap map_cos,
+                const __grid_constant__ CUtensorMap map_sin, const Params p) {
+    using S = Smem<BN, kPair, kEpi == kRope>;
     constexpr int kTileM = kPair ? 2 * kBM : kBM;
     const uint32_t rank = kPair ? cluster_ctarank() : 0u;  // 0: the CTA that issues the MMAs
     const int unit0 = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
@@ -174,6 +181,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bars[S::kAccEmpty + b], kPair ? 2 * kEpiWarps : kEpiWarps);  // one per epilogue warp
         }
         mbar_init(&bars[S::kDrain], 1);
+        mbar_init(&bars[S::kCsFull], 1);
+        mbar_init(&bars[S::kCsEmpty], kEpiWarps);
         st_shared_volatile_u32(ctl.misc + 4, 0);
         st_shared_u64(ctl.misc + 8, reinterpret_cast<uint64_t>(p.status));
         st_shared_u64(ctl.misc + 16, static_cast<uint64_t>(p.timeout_ns > 0 ? p.timeout_ns : kDefaultTimeoutNs));
@@ -185,6 +194,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tensormap(&map_a);
         prefetch_tensormap(&map_b);
         prefetch_tensormap(&map_out);
+        if constexpr (kEpi == kRope) {
+            prefetch_tensormap(&map_cos);
+            prefetch_tensormap(&map_sin);
+        }
     }
     if (warp == 2) {
         if constexpr (kPair) {
@@ -299,6 +312,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             wait_bounded(bar(S::kDrain), 0, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
             __syncwarp();
         }
+    } else if (warp == 3 && kEpi == kRope) {
+        // ------------------------------------------------ cos / sin rows of each tile
+        // (positions (m0 + r) % seq_len, r < 128: one TMA box of each table when
+        // they do not wrap past seq_len; otherwise, or for tiles with no rotated
+        // column, the epilogue reads global memory and the barrier completes empty)
+        int lt = 0, armed = -1;
+        bool ok = true;
+        for (int t = unit0; ok && t < p.tiles; t += units, ++lt) {
+            const int m0 = (t / p.tiles_n) * kTileM + static_cast<int>(rank) * kBM, n0 = (t % p.tiles_n) * BN;
+            if (lt >= 1) {
+                ok = warp_wait(bar(S::kCsEmpty), (lt - 1) & 1, ctl, FDS_STATUS_TIMEOUT_LOAD);
+                if (!ok) break;
+            }
+            const int pos0 = m0 % p.seq_len;
+            const bool tma = n0 < p.rope_cols && pos0 + kBM <= p.seq_len;
+            if (elect_one()) {
+                if (tma) {
+                    mbar_arrive_expect_tx(bar(S::kCsFull), S::kCsBytes);
+                    tma_load_2d(sbase + S::cs, &map_cos, bar(S::kCsFull), 0, pos0);
+                    tma_load_2d(sbase + S::cs + kBM * 128, &map_sin, bar(S::kCsFull), 0, pos0);
+                } else {
+                    mbar_arrive(bar(S::kCsFull));
+                }
+            }
+            __syncwarp();
+            if (tma) armed = lt;
+        }
+        if (!ok && armed >= 0) {  // aborted: the last copies issued land before the CTA exits
+            wait_bounded(bar(S::kCsFull), armed & 1, ctl, FDS_STATUS_TIMEOUT_DRAIN, false);
+            __syncwarp();
+        }
     } else if (warp >= kEpiWarp0) {
         // ------------------------------------------------ epilogue
         const int wq = warp & 3;                       // TMEM lane quarter
@@ -356,18 +400,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // tile (uncoalesced: a warp's lanes are 32 rows) and kept in
                 // registers; each 16-pair chunk goes straight into the staging
                 // box, so no whole head row is held
-                const int pos = (m0 + row) % p.seq_len;
                 float cs[32], sn[32];
+                ok = warp_wait(bar(S::kCsFull), lt & 1, ctl, FDS_STATUS_TIMEOUT_SOFTMAX);
+                if (!ok) break;
                 if (n0 + c_begin < p.rope_cols) {
-                    const float4* cr = reinterpret_cast<const float4*>(p.cos_t + static_cast<int64_t>(pos) * 64);
-                    const float4* sr = reinterpret_cast<const float4*>(p.sin_t + static_cast<int64_t>(pos) * 64);
+                    const int pos0 = m0 % p.seq_len;
+                    if (pos0 + kBM <= p.seq_len) {
+                        // this row of the staged boxes (16-byte chunk j at j ^ (row & 7))
+                        const uint32_t crow = sbase + S::cs + row * 128, srow_s = crow + kBM * 128;
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const float4 c4 = __ldg(cr + q), s4 = __ldg(sr + q);
-                        cs[4 * q] = c4.x, cs[4 * q + 1] = c4.y, cs[4 * q + 2] = c4.z, cs[4 * q + 3] = c4.w;
-                        sn[4 * q] = s4.x, sn[4 * q + 1] = s4.y, sn[4 * q + 2] = s4.z, sn[4 * q + 3] = s4.w;
+                        for (int q = 0; q < 8; ++q) {
+                            const uint32_t off = static_cast<uint32_t>(q ^ (row & 7)) << 4;
+                            const float4 c4 = ld_shared_v4f32(crow + off), s4 = ld_shared_v4f32(srow_s + off);
+                            cs[4 * q] = c4.x, cs[4 * q + 1] = c4.y, cs[4 * q + 2] = c4.z, cs[4 * q + 3] = c4.w;
+                            sn[4 * q] = s4.x, sn[4 * q + 1] = s4.y, sn[4 * q + 2] = s4.z, sn[4 * q + 3] = s4.w;
+                        }
+                    } else {
+                        const int pos = (m0 + row) % p.seq_len;
+                        const float4* cr = reinterpret_cast<const float4*>(p.cos_t + static_cast<int64_t>(pos) * 64);
+                        const float4* sr = reinterpret_cast<const float4*>(p.sin_t + static_cast<int64_t>(pos) * 64);
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            const float4 c4 = __ldg(cr + q), s4 = __ldg(sr + q);
+                            cs[4 * q] = c4.x, cs[4 * q + 1] = c4.y, cs[4 * q + 2] = c4.z, cs[4 * q + 3] = c4.w;
+                            sn[4 * q] = s4.x, sn[4 * q + 1] = s4.y, sn[4 * q + 2] = s4.z, sn[4 * q + 3] = s4.w;
+                        }
                     }
                 }
+                warp_arrive(bar(S::kCsEmpty), lane);  // the rows are in registers
                 const int sw = lane & 7;
 #pragma unroll 1
                 for (int c = c_begin; c < c_begin + BN / 2; c += 64) {

@@ -533,7 +533,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None,
     QKV projection before the attention (model.py:289).
 
     ``pair``: None (default) runs 256-row tiles over CTA pairs when x has more
-    than 128 rows and K >= 512 (not for :func:`linear_rope`); True / False force CTA pairs / one CTA per
+    than 128 rows and K >= 512; True / False force CTA pairs / one CTA per
     128-row tile (the same result bit for bit: each output element sums over K
     in the same order either way, ``tests/test_linear_gpu.py``).
     ``grid_ctas`` caps the persistent CTAs (0: one per SM)."""

@@ -237,7 +237,7 @@ FDS_API int fds_rope_attn_fwd_static(const FdsRopeArgs* args, void* stream);
 #define FDS_EPILOGUE_ACCUMULATE_F32 2
 
 /* FdsLinearArgs.cta_pair: AUTO uses 256-row tiles over clusters of two CTAs
- * when m > 128, k >= 512 and the epilogue is not ROPE (each CTA loads its own 128 rows of a and half of
+ * when m > 128 and k >= 512 (each CTA loads its own 128 rows of a and half of
  * the tile's w rows; one tensor-core operation spans both SMs), else 128-row
  * tiles on one CTA each; SINGLE / PAIR force one of the two. Both give the
  * same result bit for bit. */
