@@ -16,6 +16,11 @@ is compared with the same pipeline running the reference's own ops, on the same
 waveforms and the same noise (the pipeline draws it eagerly before each replay;
 both runs seed the CUDA generator identically).
 
+``stream_files`` (runtime.py:226-283) runs on two synthetic 120 s 16 kHz
+int16 wav files written to a temporary directory: its reader thread, pinned
+double buffers, copy stream and writer thread, one graph at the full 6000-frame
+window, and the int16 wav files it writes are compared between the two runs.
+
 Bars: our pipeline against the reference's, SNR >= 30 dB on the audio (both
 approximate the fp32 model at the fp16 bar; the random-init vocoder amplifies
 small latent differences); graph replay against eager, >= 60 dB.
@@ -24,9 +29,11 @@ small latent differences); graph replay against eager, >= 60 dB.
 import os
 import sys
 import types
+import wave
 from contextlib import contextmanager
 from pathlib import Path
 
+import numpy as np
 import pytest
 import torch
 import torch.nn.functional as Fn
@@ -151,3 +158,47 @@ def test_separate_batch_with_our_attention(ref):
     snr = O.snr_db(theirs.float().cpu(), ours.float().cpu())
     print(f"separate_batch: our attention vs the reference's, {snr:.1f} dB")
     assert snr >= 30.0, snr
+
+
+def _write_wav(path, data, rate=16000):
+    with wave.open(str(path), "wb") as handle:
+        handle.setnchannels(1)
+        handle.setsampwidth(2)
+        handle.setframerate(rate)
+        handle.writeframes(data.astype(np.int16).tobytes())
+
+
+def _read_wav(path):
+    with wave.open(str(path), "rb") as handle:
+        return np.frombuffer(handle.readframes(handle.getnframes()), dtype=np.int16)
+
+
+def test_stream_files_with_our_attention(ref, tmp_path):
+    M, R, RM, W = ref
+    bundle = _bundle(RM, W, seed=2)
+    model = M.TritonModel(bundle, max_seq=R.SEQ)
+    rng = np.random.default_rng(3)
+    paths = []
+    for i in range(2):  # two full 120 s windows, 16 kHz mono int16
+        p = tmp_path / f"call{i}.wav"
+        _write_wav(p, np.clip(rng.normal(0.0, 3000.0, R.SAMPLES), -32768, 32767))
+        paths.append(p)
+    outs = {}
+    for name in ("theirs", "ours"):
+        out_dir = tmp_path / name
+        torch.cuda.manual_seed(11)  # the noise run_chain draws before each window
+        if name == "ours":
+            with _our_attention(M):
+                R.stream_files(R.TritonPipeline(None, model=model, bucket_seconds=10), paths, out_dir)
+        else:
+            R.stream_files(R.TritonPipeline(None, model=model, bucket_seconds=10), paths, out_dir)
+        outs[name] = {f.name: _read_wav(f) for f in sorted(out_dir.glob("*.wav"))}
+    F.check_status()
+    assert sorted(outs["ours"]) == sorted(outs["theirs"]) == [f"call{i}_spk{s}.wav" for i in range(2) for s in (0, 1)]
+    for fname, a in outs["theirs"].items():
+        b = outs["ours"][fname]
+        assert a.shape == b.shape == (R.OUT_SAMPLES,)
+        assert np.abs(a).max() > 100, fname  # the audio is not silent at int16 resolution
+        snr = O.snr_db(torch.from_numpy(a.astype(np.float32)), torch.from_numpy(b.astype(np.float32)))
+        print(f"stream_files {fname}: our attention vs the reference's, {snr:.1f} dB")
+        assert snr >= 30.0, (fname, snr)
