@@ -820,7 +820,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                         "frac": round((both_ms / world) / e2e_value, 3),
                         "note": "the same pinned buffers copied with no kernel (h2d alone, d2h alone, both at "
                                 "once on every rank); e2e is copy-bound when frac is near 1"}},
-            "gpu_launches": K * ENC_LAYERS,
+            "gpu_launches": K * ENC_LAYERS * world,
             "clocks": clocks.summary(),
             "e2e_layer": {
                 "value": round(el_ms / (el["steps"] * world), 4), "unit": UNIT,
@@ -836,11 +836,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             dsteps = dit[1]
             dper_ms = dms / (dsteps * DIT_LAYERS)
             line["dit"] = {"workload": "config4: 8-layer DiT RoPE attention, L=6000, 12 x 64 heads",
-                           "ms_per_window": round(dms / dsteps, 4), "median_ms_per_window": round(dit[2], 4),
+                           "ms_per_window": round(dms / (dsteps * world), 4),
+                           "ms_per_window_per_gpu": round(dms / dsteps, 4),
+                           "median_ms_per_window_per_gpu": round(dit[2], 4),
                            "tflops": round(FLOP_DIT_LAYER / (dper_ms * 1e-3) / 1e12, 1),
                            "frac": round(FLOP_DIT_LAYER / (dper_ms * 1e-3) / 1e12 / peak, 4),
                            "steps": dsteps, "launches_per_window": 2 * DIT_LAYERS,
-                           "rotated_ms_per_window": round(rms / dsteps, 4),
+                           "rotated_ms_per_window": round(rms / (dsteps * world), 4),
                            "rotated_note": "q | k rotated by the QKV projection's epilogue (linear_rope): "
                                            "8 attention launches, no RoPE pass"}
         if c3:
