@@ -287,41 +287,58 @@ __device__ __forceinline__ Item unit_item(const AttnParams& p, int u) {
 
 // Relative cost of one KV tile step of a unit with two / one query tiles (the
 // last wave is cut by these weights; one-tile units run one softmax warpgroup
-// and take about 3/5 of the time).
+// and take about 3/5 of the time), and of starting a unit's item: its Q load,
+// Q.rel^T and table fill, pipeline ramp and part epilogue, so that a piece
+// that starts a second unit gets fewer tiles. An extra item cost a piece ~10 us
+// on a B200 (7 tile steps of a two-tile unit); as a weight, 4 tile steps (20)
+// cut the encoder layer at L = 6000 best (0.2070 ms unweighted; 10: 0.2062,
+// 15: 0.2059, 20: 0.2042-0.2051, 25: 0.2048-0.2051, 35: 0.2053, 50: 0.2052).
+// The start weight is capped at a sixth of a unit's tile weight, so that short
+// units still split into pieces.
 constexpr uint32_t kWeightTwoTiles = 5;
 constexpr uint32_t kWeightOneTile = 3;
+constexpr uint32_t kWeightUnitStart = 20;
+__host__ __device__ constexpr uint32_t unit_start_weight(uint32_t n_tiles) {
+    return n_tiles * kWeightTwoTiles / 6 < kWeightUnitStart ? n_tiles * kWeightTwoTiles / 6 : kWeightUnitStart;
+}
 
-// Geometry of the (unit, KV tile) sequence: per (window, head) R units of n
-// tiles, the last unit weighted w_last per tile (a one-tile unit when the last
-// row block holds at most 128 rows), the others kWeightTwoTiles. 32-bit
-// arithmetic: the host splits the last wave only when the total weight times
-// the piece count stays below 2^31.
+// Geometry of the (unit, KV tile) sequence: per (window, head) R units, each a
+// start of weight c0 = unit_start_weight(n) then n tiles, the last unit weighted w_last
+// per tile (a one-tile unit when the last row block holds at most 128 rows),
+// the others kWeightTwoTiles. 32-bit arithmetic: the host splits the last wave
+// only when the total weight times the piece count stays below 2^31.
 struct TileSeq {
-    uint32_t n, R, w_last;
+    uint32_t n, R, w_last, c0;
     __device__ __forceinline__ explicit TileSeq(const AttnParams& p) {
         n = (p.seq_len + kBlockN - 1) / kBlockN;
         R = p.row_blocks;
         w_last = (R - 1) * kRowsPerCta + kBlockM < static_cast<uint32_t>(p.seq_len) ? kWeightTwoTiles : kWeightOneTile;
+        c0 = unit_start_weight(n);
     }
-    __device__ __forceinline__ uint32_t per_bh() const { return n * ((R - 1) * kWeightTwoTiles + w_last); }
+    __device__ __forceinline__ uint32_t unit_full() const { return c0 + n * kWeightTwoTiles; }
+    __device__ __forceinline__ uint32_t per_bh() const { return (R - 1) * unit_full() + c0 + n * w_last; }
     // weight before unit u
     __device__ __forceinline__ uint32_t unit_pos(uint32_t u) const {
         const uint32_t bh = u / R;
-        return bh * per_bh() + (u - bh * R) * n * kWeightTwoTiles;
+        return bh * per_bh() + (u - bh * R) * unit_full();
     }
-    // global tile step (unit * n + tile) at weight position x
+    // global tile step (unit * n + tile) at weight position x (a position in a
+    // unit's start maps to its first tile)
     __device__ __forceinline__ uint32_t tile_at(uint32_t x) const {
-        const uint32_t full = n * (R - 1) * kWeightTwoTiles;
+        const uint32_t full = (R - 1) * unit_full();
         const uint32_t bh = x / per_bh();
         const uint32_t rem = x - bh * per_bh();
-        uint32_t r, t;
+        uint32_t r, q, w;
         if (rem < full) {
-            r = rem / (n * kWeightTwoTiles);
-            t = (rem - r * n * kWeightTwoTiles) / kWeightTwoTiles;
+            r = rem / unit_full();
+            q = rem - r * unit_full();
+            w = kWeightTwoTiles;
         } else {
             r = R - 1;
-            t = (rem - full) / w_last;
+            q = rem - full;
+            w = w_last;
         }
+        const uint32_t t = q < c0 ? 0 : (q - c0) / w;
         return (bh * R + r) * n + t;
     }
 };

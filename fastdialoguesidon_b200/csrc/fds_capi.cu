@@ -263,7 +263,8 @@ struct Plan {
 // and the remaining units cut by weight into G pieces such that every piece
 // touches at most kMaxItems (3) units and every cut unit has at most kMaxParts
 // (4) parts: the piece weight is between a third of a two-tile unit (and at
-// least one tile) and twice the lightest unit. With grid_ctas == 0 it is used only when whole units leave
+// least a unit start and one tile) and twice the lightest unit (units weighted
+// with their start cost, attn_kernel.cuh TileSeq). With grid_ctas == 0 it is used only when whole units leave
 // more than 3% of the SM time of the waves idle.
 Plan plan_schedule(int64_t batch, int64_t heads, int64_t seq_len, bool has_kv_len, bool has_ws, int64_t ws_bytes,
                    int64_t grid_ctas, int64_t sms) {
@@ -275,16 +276,17 @@ Plan plan_schedule(int64_t batch, int64_t heads, int64_t seq_len, bool has_kv_le
     const int64_t waves = (U + G - 1) / G;
     if (grid_ctas == 0 && static_cast<double>(U) / static_cast<double>(waves * G) >= 0.97) return plan;
     const int64_t n = (seq_len + fds::kBlockN - 1) / fds::kBlockN;
-    const int64_t w2 = fds::kWeightTwoTiles;
+    const int64_t w2 = fds::kWeightTwoTiles, c0 = fds::unit_start_weight(static_cast<uint32_t>(n));
     const int64_t w_last = (R - 1) * fds::kRowsPerCta + fds::kBlockM < seq_len ? w2 : fds::kWeightOneTile;
-    const int64_t per_bh = n * ((R - 1) * w2 + w_last);
+    const int64_t unit_full = c0 + n * w2, unit_last = c0 + n * w_last;  // unit weights (attn_kernel.cuh TileSeq)
+    const int64_t per_bh = (R - 1) * unit_full + unit_last;
     const int64_t whole = (waves - 1) * G;
-    const auto unit_pos = [&](int64_t u) { return (u / R) * per_bh + (u % R) * n * w2; };
+    const auto unit_pos = [&](int64_t u) { return (u / R) * per_bh + (u % R) * unit_full; };
     const int64_t total = unit_pos(U);
     const int64_t wt = total - unit_pos(whole);
     const int64_t w_min = wt / G, w_max = (wt + G - 1) / G;
-    const bool ok = ws_bytes >= ws_bytes_for(G) && w_min >= w2 && 3 * w_min >= n * w2 && w_max <= 2 * n * w_last &&
-                    G * total < (int64_t{1} << 31);
+    const bool ok = ws_bytes >= ws_bytes_for(G) && w_min >= c0 + w2 && 3 * w_min >= unit_full &&
+                    w_max <= 2 * unit_last && G * total < (int64_t{1} << 31);
     if (ok) plan = Plan{whole + G, whole, G};
     return plan;
 }

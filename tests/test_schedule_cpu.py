@@ -23,6 +23,11 @@ from fastdialoguesidon_b200 import _native as N
 K_BLOCK = 128
 ROWS_PER_CTA = 256
 W2, W1 = 5, 3          # kWeightTwoTiles, kWeightOneTile
+C0_MAX = 20            # kWeightUnitStart: the weight of starting a unit, capped at n * W2 / 6
+
+
+def c0_of(n):
+    return min(C0_MAX, n * W2 // 6)
 MAX_ITEMS = 3          # kMaxItems
 MAX_PARTS = 4          # kMaxParts
 SLOT_BYTES = 256 * 68 * 4
@@ -33,23 +38,24 @@ def geometry(batch, heads, L):
     n = math.ceil(L / K_BLOCK)
     U = batch * heads * R
     w_last = W2 if (R - 1) * ROWS_PER_CTA + 128 < L else W1
-    per_bh = n * ((R - 1) * W2 + w_last)
+    per_bh = (R - 1) * (c0_of(n) + n * W2) + c0_of(n) + n * w_last
     return R, n, U, w_last, per_bh
 
 
 def unit_pos(u, R, n, per_bh):
-    return (u // R) * per_bh + (u % R) * n * W2
+    return (u // R) * per_bh + (u % R) * (c0_of(n) + n * W2)
 
 
 def tile_at(x, R, n, w_last, per_bh):
-    full = n * (R - 1) * W2
+    c0 = c0_of(n)
+    full = (R - 1) * (c0 + n * W2)
     bh, rem = divmod(x, per_bh)
     if rem < full:
-        r = rem // (n * W2)
-        t = (rem - r * n * W2) // W2
+        r, q = divmod(rem, c0 + n * W2)
+        w = W2
     else:
-        r = R - 1
-        t = (rem - full) // w_last
+        r, q, w = R - 1, rem - full, w_last
+    t = 0 if q < c0 else (q - c0) // w
     return (bh * R + r) * n + t
 
 
@@ -68,7 +74,9 @@ def plan(batch, heads, L, G, forced=True, has_ws=True, has_kv=False):
     total = unit_pos(U, R, n, per_bh)
     wt = total - unit_pos(whole, R, n, per_bh)
     w_min, w_max = wt // G, -(-wt // G)
-    if w_min >= W2 and 3 * w_min >= n * W2 and w_max <= 2 * n * w_last and G * total < 2 ** 31:
+    c0 = c0_of(n)
+    if (w_min >= c0 + W2 and 3 * w_min >= c0 + n * W2 and w_max <= 2 * (c0 + n * w_last)
+            and G * total < 2 ** 31):
         return whole + G, whole, G
     return U, U, 0
 
@@ -128,7 +136,7 @@ def check_plan(batch, heads, L, G):
                 assert (u, t) not in owner
                 owner[(u, t)] = whole + k
             cover.setdefault(u, []).append(k)
-            w += (te - tb) * (w_last if u % R == R - 1 else W2)
+            w += (te - tb) * (w_last if u % R == R - 1 else W2) + (c0_of(n) if tb == 0 else 0)
         weights.append(w)
     assert len(owner) == U * n
     for u, ks in cover.items():
@@ -136,7 +144,7 @@ def check_plan(batch, heads, L, G):
         if len(ks) > 1:
             for k in ks:
                 assert neighbour_parts(k, u, whole, P, batch, heads, L) == (ks[0], ks[-1])
-    assert max(weights) - min(weights) <= 2 * W2
+    assert max(weights) - min(weights) <= 2 * (W2 + c0_of(n))
 
 
 CASES = [(1, 6000, 16, 148), (1, 6000, 16, 100), (1, 1000, 16, 5), (1, 1000, 16, 37), (1, 1000, 16, 64),
