@@ -819,13 +819,26 @@ __device__ __forceinline__ void finish_part(const AttnParams& p, const float (&o
         mine[c * kRowsPerCta] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
     mine[16 * kRowsPerCta] = make_float4(m, l, 0.f, 0.f);
 
-    // pieces touching unit u: contiguous, around this one
+    // pieces touching unit u: contiguous, around this one, at most kMaxParts - 1
+    // on either side. Lane j evaluates piece k - (kMaxParts - 1) + j (its tile
+    // range: a few integer divisions), so the warp searches all candidates at
+    // once instead of every lane walking them one after another.
     const uint32_t lo_tile = static_cast<uint32_t>(u) * ts.n, hi_tile = lo_tile + ts.n;
+    constexpr int kSide = kMaxParts - 1;
+    const int kc = static_cast<int>(k) - kSide + lane;
+    uint2 rg = make_uint2(0u, 0u);
+    bool touch = false;
+    if (lane <= 2 * kSide && kc >= 0 && kc < p.pieces) {
+        rg = piece_range(p, ts, static_cast<uint32_t>(kc));
+        touch = lane < kSide ? rg.y > lo_tile : (lane > kSide ? rg.x < hi_tile : true);
+    }
+    const uint32_t near = __ballot_sync(0xffffffffu, touch);
     uint32_t k_first = k, k_last = k;
-    while (k_first > 0 && k - k_first + 1 < kMaxParts && piece_range(p, ts, k_first - 1).y > lo_tile) --k_first;
-    while (k_last + 1 < static_cast<uint32_t>(p.pieces) && k_last - k + 1 < kMaxParts &&
-           piece_range(p, ts, k_last + 1).x < hi_tile)
-        ++k_last;
+#pragma unroll
+    for (int d = 1; d <= kSide; ++d) {  // the runs of touching pieces below and above k
+        if (k_first + d == k + 1 && ((near >> (kSide - d)) & 1u)) --k_first;
+        if (k_last + 1 == k + d && ((near >> (kSide + d)) & 1u)) ++k_last;
+    }
     const uint32_t nparts = k_last - k_first + 1;
 
     uint32_t* count = p.counts + static_cast<int64_t>(u - p.whole_ctas) * kSoftmaxWarps + group;
@@ -845,7 +858,8 @@ __device__ __forceinline__ void finish_part(const AttnParams& p, const float (&o
     for (int c = 0; c < 64; ++c) acc[c] = 0.f;
     // (this part's own rows are read back from its slot too: no registers held)
     for (uint32_t kk = k_first; kk <= k_last; ++kk) {
-        const uint32_t first_unit = piece_range(p, ts, kk).x / ts.n;
+        // piece kk's first tile, from the lane that evaluated it above
+        const uint32_t first_unit = __shfl_sync(0xffffffffu, rg.x, static_cast<int>(kk - k) + kSide) / ts.n;
         const float4* part = slot(kk, static_cast<uint32_t>(u) - first_unit);
         const float4 ml = __ldcg(part + 16 * kRowsPerCta);
         float4 v[16];
